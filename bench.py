@@ -1,0 +1,370 @@
+"""Benchmark of the SageAttention hot path on B200: the Wan-2.1-14B 480p self-attention call.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--strong]
+
+One step = one sageattention.sageattn call (V amax, Q quantiser, K+V quantiser, int8/fp8 attention) on
+B=1, H=40, N=32760, D=128, bf16, NHD, K ~ N(0,1) + per-channel offset N(0, std 2).  Inputs (1.0 GB) are
+larger than the 126 MB L2, so consecutive steps do not hit in L2.
+
+Prints one JSON line (rank 0):
+  value      effective TOPS (4*B*H*N^2*D / time) of the whole job, inputs resident in HBM, CUDA events
+  e2e        same metric through the public API with pinned host inputs copied in and the output copied
+             out inside every step
+  roofline   the attention kernel timed alone (CUDA events around sage_attn_fwd) against the dense
+             8-bit tensor peak = 2 x the measured bf16 cuBLAS peak in MEASURED_PEAKS.json
+  cpu_baseline  the reference's CPU path for this call (torch SDPA in bf16 on the host cores, the route
+             the reference takes off-GPU) on a head subset, scaled by operations
+N > 1 (torchrun, one rank per GPU): each rank runs its own (batch, head) units with no collective
+(weak scaling: global batch = N Wan calls); --strong instead splits the 40 heads of one call.
+--impl reference times only the CPU path (rank 0; other ranks exit 0).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "rdna4-sageattention_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+B, H, N, D = 1, 40, 32760, 128
+REF_WAN_MS = 158.0          # reference README.md:194, Wan 2.1 14B 480p, RX 9070 XT, ms per call
+METRIC = "ms/call & TOPS per GPU, 32760-tok 40-head d128 sageattn; % int8/fp8 TC peak"
+
+
+def ops_per_call(b=B, h=H, n=N, d=D):
+    return 4.0 * b * h * n * n * d
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(device, b=B, h=H, n=N, d=D, seed=0):
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn((b, n, h, d), device=device, dtype=torch.bfloat16, generator=g)
+    k = torch.randn((b, n, h, d), device=device, dtype=torch.float32, generator=g)
+    k = (k + torch.randn((d,), device=device, generator=g) * 2.0).to(torch.bfloat16)
+    v = torch.randn((b, n, h, d), device=device, dtype=torch.bfloat16, generator=g)
+    return q, k, v
+
+
+def cpu_baseline(seconds_target=12.0):
+    """The reference's CPU path (oracle restatement of src/rdna4_sage/__init__.py:44-58) on a head subset."""
+    from oracle import sage_oracle as O
+
+    heads = 1
+    q, k, v = make_inputs("cpu", h=heads)
+    t0 = time.perf_counter()
+    O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+    one = time.perf_counter() - t0
+    reps = max(1, min(8, int(seconds_target / max(one, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": ops_per_call(h=heads) / dt / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{heads} of {H} heads (B=1 N={N} D={D} bf16 NHD) x {reps} through the reference's SDPA "
+                      f"fallback on CPU; {dt * 1e3:.0f} ms per head-call, scaled by operations "
+                      f"(full call ~ {dt * H:.1f} s)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import sage_oracle as O
+
+    heads = 1
+    q, k, v = make_inputs("cpu", h=heads)
+    for _ in range(args.warmup):
+        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = ops_per_call(h=heads) / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 * H / heads,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16)",
+                       "global_batch": 1, "seq_len": N, "parallelism": "host cores"},
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{heads} of {H} heads per step through the reference's SDPA fallback on "
+                                       f"CPU (torch bf16 SDPA), ms_per_step scaled to the full 40-head call"},
+            "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import rdna4_sage
+    import sageattention
+    from rdna4_sage import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    heads = H
+    if args.strong and world > 1:
+        heads = H // world + (1 if rank < H % world else 0)
+    q, k, v = make_inputs(dev, h=heads, seed=rank)
+    ops = ops_per_call(h=heads)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return sageattention.sageattn(q, k, v, tensor_layout="NHD")
+
+    assert rdna4_sage.is_available() and rdna4_sage._worth_it(q, k, "NHD")
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: inputs resident in HBM
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+    rdna4_sage._attention.check_status(dev)
+    total_ops = ops_per_call() if args.strong else ops * world
+    value = total_ops / (ms * 1e-3) / 1e12
+
+    # ---- e2e: public API with pinned host buffers, copies inside every step
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        o = sageattention.sageattn(dq, dk, dv, tensor_layout="NHD")
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(max(2, args.steps // 2)):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / max(2, args.steps // 2))
+    del hq, hk, hv, hout
+
+    # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream)
+    L = _lib.lib()
+    Bq, Sq, Hq, Dq = q.shape
+    spad = (Sq + 31) // 32 * 32
+    ws_bytes = L.sage_workspace_bytes(Bq, Hq, Hq, Sq, Sq, Dq)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    dk_ = L.sage_qk_row_bytes(Dq)
+    out = torch.empty((Bq, Sq, Hq, Dq), device=dev, dtype=q.dtype)
+    off = 0
+
+    def take(nbytes):
+        nonlocal off
+        p = ws.data_ptr() + off
+        off += (nbytes + 255) // 256 * 256
+        return p
+
+    q8 = take(Bq * Hq * Sq * dk_)
+    qs = take(Bq * Hq * Sq * 4)
+    k8 = take(Bq * Hq * spad * dk_)
+    ks = take(Bq * Hq * spad // 32 * 4)
+    v8t = take(Bq * Hq * Dq * spad)
+    vs = take(Bq * Hq * Dq * 4)
+    st = stream.cuda_stream
+    sq = (q.stride(0), q.stride(1), q.stride(2))
+
+    def quant():
+        _lib.check(L.sage_v_amax(v.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, vs, st), "v_amax")
+        _lib.check(L.sage_quant_q(q.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, 1.0, q8, qs, st), "quant_q")
+        _lib.check(L.sage_quant_kv(k.data_ptr(), v.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, *sq, vs, k8, ks, v8t, st),
+                   "quant_kv")
+
+    def attn():
+        _lib.check(L.sage_attn_fwd(q8, qs, k8, ks, v8t, vs, out.data_ptr(), 0, Bq, Hq, Hq, Sq, Sq, Dq, 0,
+                                   out.stride(0), out.stride(1), out.stride(2), None, None, st), "attn_fwd")
+
+    quant()
+    attn()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        attn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = e0.elapsed_time(e1) / args.steps
+    e0.record(stream)
+    for _ in range(args.steps):
+        quant()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    quant_ms = e0.elapsed_time(e1) / args.steps
+    peaks, peak_kind = load_peaks()
+    peak_tops = 2.0 * peaks["bf16_tflops_sustained"]
+    achieved = ops / (attn_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "attn_wan_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    elems = Bq * Sq * Hq * Dq
+    quant_bytes = 3 * elems * 2 + 3 * elems + (Bq * Hq * Sq + Bq * Hq * spad // 32 + Bq * Hq * Dq) * 4
+    quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak",
+            "vs_baseline": value / (ops_per_call() / (REF_WAN_MS * 1e-3) / 1e12),
+            "vs_baseline_basis": "value / 139.1 TOPS (reference README.md:194: 158 ms/call for this shape on "
+                                 "RX 9070 XT)",
+            "dtype": "int8 QK / e4m3 PV (bf16 in, bf16 out)", "data": "synthetic",
+            "config": {"workload": "wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16, "
+                                   "K + per-channel offset N(0, std 2))",
+                       "model": "wan2.1-14b-480p", "global_batch": 1 if args.strong else world, "seq_len": N,
+                       "heads_per_rank": heads,
+                       "parallelism": (f"heads split over {world} ranks" if args.strong else
+                                       f"dp{world}: one call's (batch, head) units per rank, no collective"),
+                       "l2": "inputs 1.0 GB per rank > 126 MB L2 (no flush needed)"},
+            "clocks": clocks.summary(),
+            "e2e": {"value": total_ops / (ms_e2e * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 4 * args.steps,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
+                         "frac": achieved / peak_tops, "traffic": traffic,
+                         "kernel": "sage_attn_kernel<128,false>", "ms_per_launch": attn_ms,
+                         "peak_basis": f"2 x bf16_tflops_sustained of {peak_kind} MEASURED_PEAKS.json "
+                                       "(dense 8-bit tensor rate = 2 x bf16 on B200)"},
+            "roofline_quant": {"bound": "hbm", "achieved": quant_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                               "frac": quant_gbs / peaks["hbm_gbs"], "ms_per_call": quant_ms,
+                               "algorithmic_bytes": quant_bytes,
+                               "kernels": "v_amax + quant_q + quant_kv (algorithmic bytes exclude the amax re-read)"},
+        }
+        if not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline() if world == 1 else None
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--strong", action="store_true", help="split the heads of one call across ranks")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

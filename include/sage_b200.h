@@ -1,0 +1,100 @@
+/* sage_b200.h: C ABI of the B200 (sm_100a) SageAttention library, libsage_b200.so.
+ *
+ * This is the native boundary that replaces the reference's launch layer: src/rdna4_sage/_hip.py
+ * (ctypes over hipModuleLoadData / hipModuleGetFunction / hipModuleLaunchKernel, _hip.py:52-73) and
+ * the three kernel launches plus V-amax pass of src/rdna4_sage/_attention.py:97-140.  Each entry point
+ * below names the reference call it replaces.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers, int sizes, int64 element strides; no allocation inside the library: the
+ *     caller owns every buffer (the reference allocates with torch, _attention.py:115-119,133);
+ *   - work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream) and not waited for;
+ *   - return 0 on success or a SAGE_* status; sage_last_error() gives the message (thread-local);
+ *   - dtype: SAGE_BF16 or SAGE_F16 for the 16-bit inputs/outputs;
+ *   - strides are in elements, for the (batch, sequence, head) axes; the channel axis is contiguous.
+ *     Pointers and the three strides must be 16-byte aligned (8 elements), as the reference's
+ *     _bsh (_attention.py:59-67) guarantees for its kernels.
+ *
+ * Quantised tensor layouts exchanged between the entry points (heads outermost per batch):
+ *   q8  [B, H,   Sq,      DK] int8   DK = sage_qk_row_bytes(D), columns >= D zero
+ *   qs  [B, H,   Sq]          float  per-token scale / RB times the sm_scale fold
+ *   k8  [B, Hkv, Skv_pad, DK] int8   Skv_pad = ceil(Skv / 32) * 32, pad rows zero
+ *   ks  [B, Hkv, Skv_pad/32]  float  one scale per 32-key block
+ *   v8t [B, Hkv, D, Skv_pad]  e4m3   V transposed, pad keys zero
+ *   vs  [B, Hkv, D]           float  per-channel max |V|
+ */
+#ifndef SAGE_B200_H
+#define SAGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAGE_B200_ABI_VERSION 1
+
+enum { SAGE_BF16 = 0, SAGE_F16 = 1 };
+
+enum {
+  SAGE_OK = 0,
+  SAGE_ERR_UNSUPPORTED = 1, /* shape / dtype the kernels do not handle (the reference's Unsupported) */
+  SAGE_ERR_INVALID = 2,     /* bad pointer alignment, workspace too small, ... */
+  SAGE_ERR_LAUNCH = 3,      /* CUDA runtime error at launch (the reference's RuntimeError, _hip.py:47-49) */
+  SAGE_ERR_TIMEOUT = 4      /* a kernel-side bounded wait expired (reported through the status word) */
+};
+
+/* ABI version of the loaded library (SAGE_B200_ABI_VERSION). */
+int sage_abi_version(void);
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* sage_last_error(void);
+
+/* Bytes per row of q8 / k8 for head dim D (64 -> 64, 96/128 -> 128, 256 -> 256); 0 if unsupported. */
+int sage_qk_row_bytes(int D);
+
+/* Replaces `vs = torch.linalg.vector_norm(v, ord=inf, dim=seq)` (_attention.py:121):
+ * vs[b, h, c] = max_s |V[b, s, h, c]| for V (B, S, H, D). */
+int sage_v_amax(const void* v, int dtype, int B, int S, int H, int D, int64_t sb, int64_t ss, int64_t sh, float* vs,
+                void* stream);
+
+/* Replaces the quant_q launch (_attention.py:125-126, kernel kernel_build/sage_quant.py:33-48) and the
+ * sm_scale fold (_attention.py:130-131): q8/qs from Q (B, S, H, D); `fold` multiplies qs (1 = none). */
+int sage_quant_q(const void* q, int dtype, int B, int S, int H, int D, int64_t sb, int64_t ss, int64_t sh, float fold,
+                 int8_t* q8, float* qs, void* stream);
+
+/* Replaces the quant_kv launch (_attention.py:127-129, kernel kernel_build/sage_quant.py:51-70):
+ * k8/ks/v8t from K, V (B, S, H, D) and the channel amax vs from sage_v_amax. */
+int sage_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, int64_t skb, int64_t sks,
+                  int64_t skh, int64_t svb, int64_t svs, int64_t svh, const float* vs, int8_t* k8, float* ks,
+                  uint8_t* v8t, void* stream);
+
+/* Replaces the attention launch (_attention.py:133-139; kernel make_sage_r2.py:54-269): out[b, s, h, :]
+ * (element strides osb, oss, osh) in out_dtype; optional lse [B, H, Sq] (natural log of the softmax
+ * denominator of the dequantised logits); causal is bottom-right aligned.  `status` (nullable) is a
+ * device int that receives SAGE_ERR_TIMEOUT if a kernel-side wait expires. */
+int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                  const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D, int causal,
+                  int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream);
+
+/* Workspace bytes sage_attention needs for the quantised tensors above (256-byte aligned parts). */
+size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D);
+
+/* The whole hot path of rdna4_sage._attention.attention (_attention.py:97-140) in one call:
+ * V amax, quantise Q, quantise K+V, attention.  sm_scale <= 0 selects 1/sqrt(D); any other value
+ * not within 1e-6 relative of 1/sqrt(D) is folded into the Q scales as the reference does. */
+int sage_attention(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                   int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                   int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb, int64_t oss,
+                   int64_t osh, float* lse, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* Synchronise `stream`, read and clear a status word (NULL = the library's own word on the current
+ * device); returns the code it held (SAGE_OK when no kernel reported an error). */
+int sage_status_sync(int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAGE_B200_H */

@@ -1,0 +1,503 @@
+// int8 QK^T / fp8 PV flash attention for sm_100a (tcgen05 + TMA), the B200 replacement of the
+// reference's FlyDSL attention kernel (kernel_build/make_sage.py, make_sage_r2.py:54-269,
+// make_sage_pkg.py).
+//
+// One CTA owns QT query tiles of 128 rows of one (batch, head) and walks the keys in tiles of 128:
+//   warp 4*QT      TMA producer: Q tiles once, then K (int8) and V^T (e4m3) tiles into an NST-deep ring
+//   warp 4*QT+1    MMA issuer (one thread): S_t = Q_t K^T with tcgen05.mma kind::i8 into TMEM (int32),
+//                  O_t += P_t V with kind::f8f6f4, P_t read from TMEM
+//   warps 0..4QT-1 softmax, one warpgroup per Q tile and one thread per query row: reads S_t from
+//                  TMEM, applies the per-32-key K scales, keeps the running max lazily (threshold 8 in
+//                  log2 units, as the reference), writes P_t = e4m3(exp2(...)) back into the S_t columns,
+//                  rescales O_t in TMEM when its max moved, and runs the epilogue
+// TMEM (512 columns): S/P slot 0 at column 0, slot 1 at column 128, O_t at 256 + t*D.
+// With QT = 2 (D <= 128) slot t belongs to Q tile t; with QT = 1 (D = 256) the two slots alternate
+// between consecutive key tiles so QK^T of tile j+1 overlaps the softmax of tile j.
+//
+// Arithmetic per query row i and key tile (matches the reference up to the tile width):
+//   c      = fp32(sm_scale*log2e) * qs_i
+//   for each 32-key block b of the tile, in order (the reference's tile width):
+//     m moves to max(m, max_j(s_ij) * ks_b) iff that exceeds m by more than 8 / c
+//   corr   = exp2((m_old - m_new) * c), O and l rescaled only when m moved
+//   p_ij   = exp2(fma(s_ij, c * ks_b, -c * m_new)),  l = corr * l + sum_j p_ij
+//   O     += e4m3(p) . v8,   out = O * ((1/448) / l) * vs_channel
+// Causal masks keep key j <= i + (Skv - Sq) (bottom-right aligned); keys >= Skv are masked.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "sage_internal.h"
+#include "sage_ptx.cuh"
+
+namespace sage {
+
+struct AttnParams {
+  const float* qs;
+  const float* ks;
+  const float* vs;
+  void* out;
+  float* lse;
+  int* status;
+  int64_t o_sb, o_ss, o_sh;
+  int B, H, Hkv, Sq, Skv, nkb;
+  int q_groups;  // number of QT*128-row query groups per (batch, head)
+  float sm_log2e;
+  int out_f16;
+};
+
+template <int D>
+struct AttnCfg {
+  static constexpr int QT = D <= 128 ? 2 : 1;                         // 128-row Q tiles per CTA
+  static constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);    // int8 bytes per Q/K row
+  static constexpr int SW = DK >= 128 ? 128 : 64;                     // swizzle width of a Q/K box
+  static constexpr int BM = 128;
+  static constexpr int BN = 128;
+  static constexpr int Q_TILE = BM * DK;
+  static constexpr int K_TILE = BN * DK;
+  static constexpr int V_TILE = D * BN;
+  static constexpr int NST = D == 64 ? 6 : (D == 256 ? 2 : 4);
+  static constexpr int THREADS = 128 * QT + 64;
+  static constexpr int PRODUCER_WARP = 4 * QT;
+  static constexpr int MMA_WARP = 4 * QT + 1;
+  static constexpr int O_COL = 256;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int NUM_BARS = 1 + 3 * NST + 2 + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = 1024 + QT * Q_TILE + NST * (K_TILE + V_TILE) + NUM_BARS * 8 + 16;
+  // Keep a second CTA off the SM: its tcgen05.alloc of all 512 columns would have to wait.
+  static constexpr int SMEM_ALLOC = SMEM_BYTES > 120 * 1024 ? SMEM_BYTES : 120 * 1024;
+};
+
+__device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) {
+  return (uint32_t)pack_e4m3x2(a, b) | ((uint32_t)pack_e4m3x2(c, d) << 16);
+}
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
+    sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  using C = AttnCfg<D>;
+  constexpr int QT = C::QT;
+  constexpr int NST = C::NST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + QT * C::Q_TILE;
+  uint8_t* sV = sK + NST * C::K_TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NST * C::V_TILE);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* v_full = k_full + NST;
+  uint64_t* kv_empty = v_full + NST;
+  uint64_t* s_full = kv_empty + NST;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* mma_drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
+  int* cta_abort = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  int grp = blockIdx.x % p.q_groups;
+  const int bh = blockIdx.x / p.q_groups;
+  if (CAUSAL) grp = p.q_groups - 1 - grp;  // longest key ranges first
+  const int b = bh / p.H;
+  const int h = bh - b * p.H;
+  const int hkv = h / (p.H / p.Hkv);
+  const int q0 = grp * QT * 128;
+  const int off = p.Skv - p.Sq;
+  int kv_end = p.Skv;
+  if (CAUSAL) kv_end = min(p.Skv, q0 + QT * 128 + off);
+  const int n_tiles = kv_end > 0 ? (kv_end + C::BN - 1) / C::BN : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(mma_drain, 1);
+    *cta_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const WaitCtx wc{cta_abort, p.status};
+
+  if (warp == C::PRODUCER_WARP) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      const int zq = b * p.H + h;
+      const int zk = b * p.Hkv + hkv;
+      // Q tiles wholly past the last query row are not loaded (their rows are never stored)
+      const int q_tiles_in = min(QT, (p.Sq - q0 + 127) / 128);
+      mbar_arrive_expect_tx(q_full, q_tiles_in * C::Q_TILE);
+      for (int t = 0; t < q_tiles_in; ++t)
+        for (int a = 0; a < C::DK / C::SW; ++a)
+          tma_load_3d(sQ + t * C::Q_TILE + a * C::BM * C::SW, &tm_q, q_full, a * C::SW, q0 + t * 128, zq);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % NST;
+        const uint32_t ph = (j / NST) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, wc)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], C::K_TILE);
+        for (int a = 0; a < C::DK / C::SW; ++a)
+          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, j * C::BN, zk);
+        mbar_arrive_expect_tx(&v_full[st], C::V_TILE);
+        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], j * C::BN, 0, zk);
+        issued = j + 1;
+      }
+      if (!ok) {
+        // error path: let every copy still in flight land before the CTA exits
+        mbar_drain(q_full, 0);
+        for (int jj = issued - NST > 0 ? issued - NST : 0; jj < issued; ++jj) {
+          mbar_drain(&k_full[jj % NST], (jj / NST) & 1);
+          mbar_drain(&v_full[jj % NST], (jj / NST) & 1);
+        }
+      }
+    }
+  } else if (warp == C::MMA_WARP) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t kIdescQK = idesc_i8(128, 128);
+      constexpr uint32_t kIdescPV = idesc_e4m3(128, D);
+      auto issue_s = [&](int j, int t, int slot) {
+        const int st = j % NST;
+#pragma unroll
+        for (int ks = 0; ks < C::DK / 32; ++ks) {
+          const int a = ks / (C::SW / 32);
+          const int kk = ks % (C::SW / 32);
+          const uint64_t ad = smem_desc_kmajor(smem_u32(sQ + t * C::Q_TILE + a * C::BM * C::SW) + kk * 32, C::SW);
+          const uint64_t bd = smem_desc_kmajor(smem_u32(sK + st * C::K_TILE + a * C::BN * C::SW) + kk * 32, C::SW);
+          mma_i8_ss(tmem + slot * 128, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[slot]);
+      };
+      auto issue_pv = [&](int j, int t, int slot) {
+        const int st = j % NST;
+#pragma unroll
+        for (int ks = 0; ks < C::BN / 32; ++ks) {
+          const uint64_t bd = smem_desc_kmajor(smem_u32(sV + st * C::V_TILE) + ks * 32, 128);
+          mma_f8_ts(tmem + C::O_COL + t * D, tmem + slot * 128 + ks * 8, bd, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc_commit(&o_done[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, wc) && mbar_wait(&k_full[0], 0, wc);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0, 0);
+        if (QT == 2) issue_s(0, 1, 1);
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j % NST;
+        const uint32_t ph = (j / NST) & 1;
+        const bool more = j + 1 < n_tiles;
+        const int st1 = (j + 1) % NST;
+        const uint32_t ph1 = ((j + 1) / NST) & 1;
+        if (QT == 2) {
+          if (!mbar_wait(&v_full[st], ph, wc) || !mbar_wait(&p_full[0], j & 1, wc)) break;
+          tc_fence_after();
+          issue_pv(j, 0, 0);
+          if (more) {
+            if (!mbar_wait(&k_full[st1], ph1, wc)) break;
+            tc_fence_after();
+            issue_s(j + 1, 0, 0);
+          }
+          if (!mbar_wait(&p_full[1], j & 1, wc)) break;
+          tc_fence_after();
+          issue_pv(j, 1, 1);
+          tc_commit(&kv_empty[st]);
+          if (more) issue_s(j + 1, 1, 1);
+        } else {
+          if (more) {
+            if (!mbar_wait(&k_full[st1], ph1, wc)) break;
+            tc_fence_after();
+            issue_s(j + 1, 0, (j + 1) & 1);
+          }
+          if (!mbar_wait(&v_full[st], ph, wc) || !mbar_wait(&p_full[j & 1], (j >> 1) & 1, wc)) break;
+          tc_fence_after();
+          issue_pv(j, 0, j & 1);
+          tc_commit(&kv_empty[st]);
+        }
+      }
+      // all issued MMAs complete before this thread leaves (TMEM is freed afterwards)
+      tc_commit(mma_drain);
+      mbar_drain(mma_drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int q_row = q0 + t * 128 + row;
+    const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    const float qsr = __ldg(p.qs + ((int64_t)b * p.H + h) * p.Sq + min(q_row, p.Sq - 1));
+    const float c = p.sm_log2e * qsr;
+    const float* ksb = p.ks + ((int64_t)b * p.Hkv + hkv) * p.nkb;
+    const int last_key = CAUSAL ? q_row + off : 0x7fffffff;
+    float m = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int slot = QT == 2 ? t : (j & 1);
+      const uint32_t sph = QT == 2 ? (j & 1) : ((j >> 1) & 1);
+      const int kv0 = j * C::BN;
+      float ksv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kb = j * 4 + i;
+        ksv[i] = kb < p.nkb ? __ldg(ksb + kb) : 0.f;
+      }
+      if (!mbar_wait(&s_full[slot], sph, wc)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tmem_ld32(tl + slot * 128 + i * 32, s[i]);
+      tmem_wait_ld();
+      const bool need_mask = (kv0 + C::BN > p.Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
+      const int lim = min(p.Skv, CAUSAL ? last_key + 1 : p.Skv);  // keys < lim are kept
+      // Lazy running max, decided per 32-key block in key order exactly as the reference's 32-key
+      // tiles do: the max moves only when a block's scaled max exceeds it by more than 8 / c.
+      float m_new = m;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int mx = INT32_MIN;
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (kv0 + i * 32 + e < lim) mx = max(mx, (int)s[i][e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mx = max(mx, (int)s[i][e]);
+        }
+        if (mx != INT32_MIN || !need_mask) {
+          const float cand = fmaxf(m_new, (float)mx * ksv[i]);
+          if (cand != -INFINITY && (cand - m_new) * c > 8.0f) m_new = cand;
+        }
+      }
+      const bool need = m_new != m;
+      const float corr = need ? fast_exp2((m - m_new) * c) : 1.0f;
+      const float negcm = m_new == -INFINITY ? 0.f : -(c * m_new);
+      float sum = 0.f;
+      uint32_t pw[32];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float cts = c * ksv[i];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          float pv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int idx = w * 4 + e;
+            const float sf = __int_as_float((int)s[i][idx] + kMagicI) - kMagicF;
+            float x = fast_exp2(fmaf(sf, cts, negcm));
+            if (need_mask && kv0 + i * 32 + idx >= lim) x = 0.f;
+            pv[e] = x;
+            sum += x;
+          }
+          pw[i * 8 + w] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
+        }
+      }
+      l = corr * l + sum;
+      tmem_st32(tl + slot * 128, pw);
+      if (__any_sync(0xffffffffu, need && j > 0)) {
+        // the previous P.V of this tile must have landed before O is rescaled
+        if (!mbar_wait(&o_done[t], (j - 1) & 1, wc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t o[32];
+          tmem_ld32(tl + C::O_COL + t * D + cc * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+          tmem_st32(tl + C::O_COL + t * D + cc * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[slot]);
+      m = m_new;
+    }
+    // ---------------------------------------------------------------- epilogue
+    if (ok && n_tiles > 0) ok = mbar_wait(&o_done[t], (n_tiles - 1) & 1, wc);
+    if (ok) {
+      tc_fence_after();
+      const float inv = __fdiv_rn(1.0f / 448.0f, l);
+      const float* vsp = p.vs + ((int64_t)b * p.Hkv + hkv) * D;
+      const bool store = q_row < p.Sq;
+      char* orow = reinterpret_cast<char*>(p.out) +
+                   2 * ((int64_t)b * p.o_sb + (int64_t)(store ? q_row : 0) * p.o_ss + (int64_t)h * p.o_sh);
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t o[32];
+        if (n_tiles > 0) {
+          tmem_ld32(tl + C::O_COL + t * D + cc * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float v0 = __uint_as_float(o[e]) * inv * __ldg(vsp + cc * 32 + e);
+          const float v1 = __uint_as_float(o[e + 1]) * inv * __ldg(vsp + cc * 32 + e + 1);
+          uint32_t pk;
+          if (p.out_f16) {
+            __half2 hv = __floats2half2_rn(v0, v1);
+            pk = *reinterpret_cast<uint32_t*>(&hv);
+          } else {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(v0, v1);
+            pk = *reinterpret_cast<uint32_t*>(&hv);
+          }
+          packed[e / 2] = pk;
+        }
+        if (store) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 64);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+        }
+      }
+      if (p.lse != nullptr && store)
+        p.lse[((int64_t)b * p.H + h) * p.Sq + q_row] = (m * c + log2f(l)) * 0.69314718055994531f;
+    }
+    tmem_wait_st();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D uint8 tensor map: dims {x (contiguous), y, z}, box {bx, by, 1}.
+static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
+                     uint64_t stride_z, uint32_t bx, uint32_t by, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+    return false;
+  }
+  cuuint64_t dims[3] = {x, y, z};
+  cuuint64_t strides[2] = {stride_y, stride_z};
+  cuuint32_t box[3] = {bx, by, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
+template <int D, bool CAUSAL>
+static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
+  using C = AttnCfg<D>;
+  const int64_t skv_pad = kv_pad(a.Skv);
+  CUtensorMap mq, mk, mv;
+  const CUtensorMapSwizzle qk_sw = C::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (!make_map(&mq, a.q8, C::DK, a.Sq, (uint64_t)a.B * a.H, C::DK, (uint64_t)a.Sq * C::DK, C::SW, 128, qk_sw) ||
+      !make_map(&mk, a.k8, C::DK, skv_pad, (uint64_t)a.B * a.Hkv, C::DK, (uint64_t)skv_pad * C::DK, C::SW, 128,
+                qk_sw) ||
+      !make_map(&mv, a.v8t, skv_pad, D, (uint64_t)a.B * a.Hkv, skv_pad, (uint64_t)skv_pad * D, 128, D,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return kStatusInvalid;
+  AttnParams p;
+  p.qs = a.qs;
+  p.ks = a.ks;
+  p.vs = a.vs;
+  p.out = a.out;
+  p.lse = a.lse;
+  p.status = a.status != nullptr ? a.status : default_status_word();
+  p.o_sb = a.out_st.b;
+  p.o_ss = a.out_st.s;
+  p.o_sh = a.out_st.h;
+  p.B = a.B;
+  p.H = a.H;
+  p.Hkv = a.Hkv;
+  p.Sq = a.Sq;
+  p.Skv = a.Skv;
+  p.nkb = (int)(skv_pad / kKvBlock);
+  p.q_groups = (a.Sq + C::QT * 128 - 1) / (C::QT * 128);
+  p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
+  p.out_f16 = a.out_dtype == 1;
+  auto kern = sage_attn_kernel<D, CAUSAL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  const int64_t grid = (int64_t)a.B * a.H * p.q_groups;
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("attention launch: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  return kStatusOk;
+}
+
+int launch_attention(const AttnArgs& a, cudaStream_t stream) {
+  switch (a.D) {
+    case 64: return a.causal ? launch_attention_t<64, true>(a, stream) : launch_attention_t<64, false>(a, stream);
+    case 96: return a.causal ? launch_attention_t<96, true>(a, stream) : launch_attention_t<96, false>(a, stream);
+    case 128: return a.causal ? launch_attention_t<128, true>(a, stream) : launch_attention_t<128, false>(a, stream);
+    case 256: return a.causal ? launch_attention_t<256, true>(a, stream) : launch_attention_t<256, false>(a, stream);
+    default: set_error("head_dim %d is not supported (64, 96, 128, 256)", a.D); return kStatusUnsupported;
+  }
+}
+
+}  // namespace sage

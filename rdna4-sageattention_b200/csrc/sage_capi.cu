@@ -1,0 +1,233 @@
+// extern "C" entry points of libsage_b200.so (declared in include/sage_b200.h): argument checks,
+// workspace carving and dispatch to the kernel launchers.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/sage_b200.h"
+#include "sage_internal.h"
+#include "sage_ptx.cuh"
+
+namespace sage {
+
+static thread_local char g_error[512] = {0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+// Library-owned status word, one per device (used when the caller passes no status pointer).
+__device__ int g_status_word;
+
+int* default_status_word() {
+  static std::mutex mu;
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status_word) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static int check_common(int dtype, int B, int S, int H, int D) {
+  if (dtype != SAGE_BF16 && dtype != SAGE_F16) {
+    set_error("dtype %d (SAGE_BF16 or SAGE_F16 required)", dtype);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (D != 64 && D != 96 && D != 128 && D != 256) {
+    set_error("head_dim %d (supported 64, 96, 128, 256)", D);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (B <= 0 || S <= 0 || H <= 0) {
+    set_error("empty tensor (B=%d S=%d H=%d)", B, S, H);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  return SAGE_OK;
+}
+
+static int check_input(const void* p, int64_t sb, int64_t ss, int64_t sh, const char* name) {
+  if (p == nullptr || !aligned16(p) || (sb & 7) || (ss & 7) || (sh & 7)) {
+    set_error("%s: pointer and (batch, seq, head) strides must be 16-byte aligned", name);
+    return SAGE_ERR_INVALID;
+  }
+  return SAGE_OK;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Workspace {
+  int8_t* q8;
+  float* qs;
+  int8_t* k8;
+  float* ks;
+  uint8_t* v8t;
+  float* vs;
+  size_t bytes;
+};
+
+static Workspace carve(void* base, int B, int H, int Hkv, int Sq, int Skv, int D) {
+  const size_t dk = (size_t)qk_row_bytes(D);
+  const size_t sp = (size_t)kv_pad(Skv);
+  size_t off = 0;
+  Workspace w{};
+  char* c = static_cast<char*>(base);
+  auto take = [&](size_t n) {
+    char* p = c ? c + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  w.q8 = reinterpret_cast<int8_t*>(take((size_t)B * H * Sq * dk));
+  w.qs = reinterpret_cast<float*>(take((size_t)B * H * Sq * 4));
+  w.k8 = reinterpret_cast<int8_t*>(take((size_t)B * Hkv * sp * dk));
+  w.ks = reinterpret_cast<float*>(take((size_t)B * Hkv * (sp / kKvBlock) * 4));
+  w.v8t = reinterpret_cast<uint8_t*>(take((size_t)B * Hkv * D * sp));
+  w.vs = reinterpret_cast<float*>(take((size_t)B * Hkv * D * 4));
+  w.bytes = off;
+  return w;
+}
+
+// math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)
+static bool isclose_rel(double a, double b, double rel) {
+  return std::fabs(a - b) <= rel * std::fmax(std::fabs(a), std::fabs(b));
+}
+
+}  // namespace sage
+
+using namespace sage;
+
+extern "C" {
+
+int sage_abi_version(void) { return SAGE_B200_ABI_VERSION; }
+
+const char* sage_last_error(void) { return g_error; }
+
+int sage_qk_row_bytes(int D) {
+  return (D == 64 || D == 96 || D == 128 || D == 256) ? qk_row_bytes(D) : 0;
+}
+
+int sage_v_amax(const void* v, int dtype, int B, int S, int H, int D, int64_t sb, int64_t ss, int64_t sh, float* vs,
+                void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(dtype, B, S, H, D);
+  if (rc == SAGE_OK) rc = check_input(v, sb, ss, sh, "v");
+  if (rc != SAGE_OK) return rc;
+  return launch_v_amax(v, dtype, B, S, H, D, Strides3{sb, ss, sh}, vs, static_cast<cudaStream_t>(stream));
+}
+
+int sage_quant_q(const void* q, int dtype, int B, int S, int H, int D, int64_t sb, int64_t ss, int64_t sh, float fold,
+                 int8_t* q8, float* qs, void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(dtype, B, S, H, D);
+  if (rc == SAGE_OK) rc = check_input(q, sb, ss, sh, "q");
+  if (rc == SAGE_OK && (!aligned16(q8) || qs == nullptr)) {
+    set_error("q8 must be 16-byte aligned and qs non-null");
+    rc = SAGE_ERR_INVALID;
+  }
+  if (rc != SAGE_OK) return rc;
+  return launch_quant_q(q, dtype, B, S, H, D, Strides3{sb, ss, sh}, fold, q8, qs, static_cast<cudaStream_t>(stream));
+}
+
+int sage_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, int64_t skb, int64_t sks,
+                  int64_t skh, int64_t svb, int64_t svs, int64_t svh, const float* vs, int8_t* k8, float* ks,
+                  uint8_t* v8t, void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(dtype, B, S, H, D);
+  if (rc == SAGE_OK) rc = check_input(k, skb, sks, skh, "k");
+  if (rc == SAGE_OK) rc = check_input(v, svb, svs, svh, "v");
+  if (rc == SAGE_OK && (!aligned16(k8) || !aligned16(v8t) || ks == nullptr || vs == nullptr)) {
+    set_error("k8 / v8t must be 16-byte aligned, ks and vs non-null");
+    rc = SAGE_ERR_INVALID;
+  }
+  if (rc != SAGE_OK) return rc;
+  return launch_quant_kv(k, v, dtype, B, S, H, D, Strides3{skb, sks, skh}, Strides3{svb, svs, svh}, vs, k8, ks, v8t,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                  const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D, int causal,
+                  int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(out_dtype, B, Sq, H, D);
+  if (rc != SAGE_OK) return rc;
+  if (Hkv <= 0 || H % Hkv != 0 || Skv <= 0) {
+    set_error("heads %d must be a multiple of kv heads %d and kv length %d positive", H, Hkv, Skv);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8t) || qs == nullptr || ks == nullptr || vs == nullptr) {
+    set_error("quantised operands must be 16-byte aligned and non-null");
+    return SAGE_ERR_INVALID;
+  }
+  rc = check_input(out, osb, oss, osh, "out");
+  if (rc != SAGE_OK) return rc;
+  AttnArgs a{q8, qs, k8, ks, v8t, vs, out, out_dtype, Strides3{osb, oss, osh}, lse, status, B, H, Hkv, Sq, Skv, D,
+             causal ? 1 : 0};
+  return launch_attention(a, static_cast<cudaStream_t>(stream));
+}
+
+size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D) {
+  if (sage_qk_row_bytes(D) == 0 || B <= 0 || H <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0) return 0;
+  return carve(nullptr, B, H, Hkv, Sq, Skv, D).bytes;
+}
+
+int sage_attention(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                   int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                   int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb, int64_t oss,
+                   int64_t osh, float* lse, void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  g_error[0] = 0;
+  const size_t need = sage_workspace_bytes(B, H, Hkv, Sq, Skv, D);
+  if (need == 0) {
+    int rc = check_common(dtype, B, Sq, H, D);
+    if (rc == SAGE_OK) set_error("invalid sizes (Hkv=%d Skv=%d)", Hkv, Skv);
+    return rc == SAGE_OK ? SAGE_ERR_UNSUPPORTED : rc;
+  }
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+    set_error("workspace of %zu bytes (16-byte aligned) required, got %zu", need, workspace_bytes);
+    return SAGE_ERR_INVALID;
+  }
+  const Workspace w = carve(workspace, B, H, Hkv, Sq, Skv, D);
+  float fold = 1.0f;
+  if (sm_scale > 0.0 && !isclose_rel(sm_scale, 1.0 / std::sqrt((double)D), 1e-6))
+    fold = (float)(sm_scale * std::sqrt((double)D));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = sage_v_amax(v, dtype, B, Skv, Hkv, D, vsb, vss, vsh, w.vs, s);
+  if (rc == SAGE_OK) rc = sage_quant_q(q, dtype, B, Sq, H, D, qsb, qss, qsh, fold, w.q8, w.qs, s);
+  if (rc == SAGE_OK)
+    rc = sage_quant_kv(k, v, dtype, B, Skv, Hkv, D, ksb, kss, ksh, vsb, vss, vsh, w.vs, w.k8, w.ks, w.v8t, s);
+  if (rc == SAGE_OK)
+    rc = sage_attn_fwd(w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, out, dtype, B, H, Hkv, Sq, Skv, D, causal, osb, oss, osh,
+                       lse, status, s);
+  return rc;
+}
+
+int sage_status_sync(int* status, void* stream) {
+  g_error[0] = 0;
+  int* word = status != nullptr ? status : default_status_word();
+  if (word == nullptr) {
+    set_error("no status word on this device");
+    return SAGE_ERR_LAUNCH;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpy(&host, word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemsetAsync(word, 0, sizeof(int), s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_error("status read: %s", cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  }
+  return host;
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// Host-side declarations shared by the kernel translation units and the C-ABI layer.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sage {
+
+// Geometry of the quantised tensors the kernels exchange (all per (batch, head), heads outermost):
+//   q8  [B, H,   Sq,      DK] int8   (DK = qk_row_bytes(D); columns >= D are zero)
+//   qs  [B, H,   Sq]          fp32   (per-token scale / RB * sm_scale fold)
+//   k8  [B, Hkv, Skv_pad, DK] int8   (rows >= Skv are zero)
+//   ks  [B, Hkv, Skv_pad/32]  fp32   (per 32-key block scale)
+//   v8t [B, Hkv, D, Skv_pad]  e4m3   (V transposed: channel rows of keys; keys >= Skv are zero)
+//   vs  [B, Hkv, D]           fp32   (per-channel max |V|)
+constexpr int kKvBlock = 32;
+
+inline int qk_row_bytes(int D) { return D == 64 ? 64 : (D == 256 ? 256 : 128); }
+inline int64_t kv_pad(int64_t S) { return (S + kKvBlock - 1) / kKvBlock * kKvBlock; }
+inline bool rotates(int D) { return (D & (D - 1)) == 0; }
+inline int rot_block(int D) {
+  int dp = 1;
+  while (dp < D) dp <<= 1;
+  return dp < 128 ? dp : 128;
+}
+
+struct Strides3 {
+  int64_t b, s, h;  // element strides of the batch, sequence and head axes (channel stride is 1)
+};
+
+void set_error(const char* fmt, ...);
+
+int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream);
+int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides3 st, float fold, int8_t* q8,
+                   float* qs, cudaStream_t stream);
+int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
+                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream);
+
+struct AttnArgs {
+  const int8_t* q8;
+  const float* qs;
+  const int8_t* k8;
+  const float* ks;
+  const uint8_t* v8t;
+  const float* vs;
+  void* out;
+  int out_dtype;     // 0 = bf16, 1 = f16
+  Strides3 out_st;   // element strides of out (b, s, h)
+  float* lse;        // [B, H, Sq] fp32 or null
+  int* status;       // device status word or null
+  int B, H, Hkv, Sq, Skv, D;
+  int causal;
+};
+int launch_attention(const AttnArgs& a, cudaStream_t stream);
+
+int* default_status_word();
+
+}  // namespace sage

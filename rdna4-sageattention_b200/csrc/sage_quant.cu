@@ -1,0 +1,383 @@
+// HBM-bound quantisers feeding the attention kernel, the B200 replacement of the reference's Triton
+// kernels (kernel_build/sage_quant.py:12-83) and of its torch V-amax pass (src/rdna4_sage/_attention.py:121).
+//
+// Q: x = q_row * Hm (unnormalised +-1 Hadamard over RB-wide blocks, RB = min(next_pow2(D), 128), only
+//    for power-of-two D), scale = max(amax_row(x), 1e-12) / 127, q8 = trunc(x/scale +- 0.5),
+//    qs = scale / RB * fold.                                              (sage_quant.py:33-48)
+// K: same rotation, one scale per 32-key block over the whole 32 x D tile, ks not divided by RB.
+// V: clamp(v * (448 / max(vs_c, 1e-30)), -448, 448) -> e4m3 (round to nearest even), vs_c the
+//    per-channel max |V|.                                                  (sage_quant.py:51-70)
+// The rotation is a fast Walsh-Hadamard transform in registers (one thread per token row, fp32
+// butterflies); it equals the reference's fp32-accumulated product with Hm up to fp32 summation order.
+// Each CTA stages a 128-row tile through shared memory so global loads and stores are coalesced.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sage_internal.h"
+#include "sage_ptx.cuh"
+
+namespace sage {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) {
+  return __half2float(v);
+}
+
+// In-place fast Walsh-Hadamard transform of x[0..N) (natural / Sylvester order, unnormalised).
+template <int N>
+__device__ __forceinline__ void fwht(float* x) {
+#pragma unroll
+  for (int len = 1; len < N; len <<= 1) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2 * len) {
+#pragma unroll
+      for (int j = i; j < i + len; ++j) {
+        const float a = x[j];
+        const float b = x[j + len];
+        x[j] = a + b;
+        x[j + len] = a - b;
+      }
+    }
+  }
+}
+
+// trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32.
+__device__ __forceinline__ int quant_code(float x, float scale) {
+  const float y = __fdiv_rn(x, scale);
+  const float t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
+  return __float2int_rz(t);
+}
+
+constexpr int kRows = 128;  // token rows per CTA (one per thread)
+
+// Cooperative coalesced copy of a [kRows][D] tile (rows strided by `row_stride` elements) into shared
+// memory rows of `pitch` bytes.  Rows >= valid are zero-filled.
+template <int D, typename T>
+__device__ __forceinline__ void load_tile(const T* __restrict__ src, int64_t row_stride, int valid, uint8_t* tile,
+                                          int pitch) {
+  constexpr int kChunks = D * 2 / 16;  // 16-byte chunks per row
+  for (int i = threadIdx.x; i < kRows * kChunks; i += blockDim.x) {
+    const int r = i / kChunks;
+    const int cch = i - r * kChunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < valid) v = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)r * row_stride) + cch);
+    *reinterpret_cast<uint4*>(tile + r * pitch + cch * 16) = v;
+  }
+}
+
+// Rotated (or plain, for D = 96) fp32 values of `N` consecutive channels of a smem row starting at c0.
+template <int N, typename T>
+__device__ __forceinline__ void row_values(const uint8_t* row, int c0, bool rot, float* x) {
+  const T* r = reinterpret_cast<const T*>(row) + c0;
+#pragma unroll
+  for (int i = 0; i < N; i += 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(r + i);
+    const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[i + k] = to_f32<T>(e[k]);
+  }
+  if (rot) fwht<N>(x);
+}
+
+template <int N>
+__device__ __forceinline__ float abs_max(const float* x) {
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) m = fmaxf(m, fabsf(x[i]));
+  return m;
+}
+
+template <int N>
+__device__ __forceinline__ void store_codes(const float* x, float scale, int8_t* dst) {
+#pragma unroll
+  for (int i = 0; i < N; i += 16) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c0 = quant_code(x[i + 4 * k + 0], scale);
+      const int c1 = quant_code(x[i + 4 * k + 1], scale);
+      const int c2 = quant_code(x[i + 4 * k + 2], scale);
+      const int c3 = quant_code(x[i + 4 * k + 3], scale);
+      w[k] = (uint32_t)(c0 & 0xff) | ((uint32_t)(c1 & 0xff) << 8) | ((uint32_t)(c2 & 0xff) << 16) |
+             ((uint32_t)(c3 & 0xff) << 24);
+    }
+    *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// Quantise one smem row (thread-private) to DK int8 codes with scale = max(rowmax, floor)/127, where
+// the scale's amax comes from `amax_fn` (the row's own amax for Q, the 32-row block amax for K).
+// D = 256 is two independent 128-wide rotation blocks sharing one scale; the first block is
+// recomputed after the scale is known so that only 128 values are live at a time.
+template <int D, typename T, typename AmaxFn>
+__device__ __forceinline__ float quant_row(const uint8_t* row, int8_t* out_row, AmaxFn amax_fn) {
+  constexpr bool kRot = (D & (D - 1)) == 0;
+  constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+  if constexpr (D == 256) {
+    float x[128];
+    row_values<128, T>(row, 0, true, x);
+    const float a0 = abs_max<128>(x);
+    row_values<128, T>(row, 128, true, x);
+    const float a1 = abs_max<128>(x);
+    const float scale = __fdiv_rn(fmaxf(amax_fn(fmaxf(a0, a1)), 1e-12f), 127.0f);
+    store_codes<128>(x, scale, out_row + 128);
+    row_values<128, T>(row, 0, true, x);
+    store_codes<128>(x, scale, out_row);
+    return scale;
+  } else {
+    float x[DK];
+    row_values<D, T>(row, 0, kRot, x);
+#pragma unroll
+    for (int i = D; i < DK; ++i) x[i] = 0.f;
+    const float scale = __fdiv_rn(fmaxf(amax_fn(abs_max<D>(x)), 1e-12f), 127.0f);
+    store_codes<DK>(x, scale, out_row);
+    return scale;
+  }
+}
+
+template <int D>
+constexpr int tile_pitch() {
+  return D * 2 + 16;  // bytes; the 16-byte skew keeps per-thread row reads free of bank conflicts
+}
+
+// ------------------------------------------------------------------------------------------------
+// Q
+// ------------------------------------------------------------------------------------------------
+template <int D, typename T>
+__global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
+                                                        float fold, int8_t* __restrict__ q8, float* __restrict__ qs) {
+  constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+  constexpr int PITCH = tile_pitch<D>();
+  extern __shared__ __align__(16) uint8_t qsm[];
+  uint8_t* tile = qsm;
+  int8_t* codes = reinterpret_cast<int8_t*>(qsm + kRows * PITCH);
+  const int s0 = blockIdx.x * kRows;
+  const int bh = blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int valid = min(kRows, S - s0);
+  load_tile<D, T>(x + (int64_t)b * st.b + (int64_t)s0 * st.s + (int64_t)h * st.h, st.s, valid, tile, PITCH);
+  __syncthreads();
+  const int r = threadIdx.x;
+  float scale = quant_row<D, T>(tile + r * PITCH, codes + r * DK, [](float a) { return a; });
+  if (r < valid) {
+    float s = scale;
+    if ((D & (D - 1)) == 0) s = s / (float)(D < 128 ? D : 128);
+    qs[(int64_t)bh * S + s0 + r] = s * fold;
+  }
+  __syncthreads();
+  // rows of one (b, h) are contiguous in q8: the CTA's output is one block of valid*DK bytes
+  int8_t* dst = q8 + ((int64_t)bh * S + s0) * DK;
+  for (int i = threadIdx.x; i < valid * DK / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(codes)[i];
+}
+
+// ------------------------------------------------------------------------------------------------
+// K + V
+// ------------------------------------------------------------------------------------------------
+template <int D, typename T>
+__global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
+                                                         int H, Strides3 sk, Strides3 sv, const float* __restrict__ vs,
+                                                         int8_t* __restrict__ k8, float* __restrict__ ks,
+                                                         uint8_t* __restrict__ v8t) {
+  constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+  constexpr int PITCH = tile_pitch<D>();
+  extern __shared__ __align__(16) uint8_t kvsm[];
+  uint8_t* tile = kvsm;                                             // K tile, then V tile
+  int8_t* codes = reinterpret_cast<int8_t*>(kvsm + kRows * PITCH);  // [kRows][DK]
+  uint8_t* vt = kvsm + kRows * PITCH + kRows * DK;                  // [D][kRows] e4m3
+  float* fac = reinterpret_cast<float*>(vt + D * kRows);            // [D]
+  const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
+  const int s0 = blockIdx.x * kRows;
+  const int bh = blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int valid = max(0, min(kRows, S - s0));
+  const int rows_out = min(kRows, spad - s0);  // rows of this tile inside the padded tensors
+  const int r = threadIdx.x;
+  const int lane = r & 31;
+
+  for (int c = threadIdx.x; c < D; c += blockDim.x)
+    fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
+
+  // K: one scale per 32-key block = one warp
+  load_tile<D, T>(k + (int64_t)b * sk.b + (int64_t)s0 * sk.s + (int64_t)h * sk.h, sk.s, valid, tile, PITCH);
+  __syncthreads();
+  const float kscale = quant_row<D, T>(tile + r * PITCH, codes + r * DK, [](float a) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
+  });
+  if (lane == 0 && r < rows_out) ks[(int64_t)bh * (spad / kKvBlock) + (s0 + r) / kKvBlock] = kscale;
+  __syncthreads();
+  {
+    int8_t* dst = k8 + ((int64_t)bh * spad + s0) * DK;
+    for (int i = threadIdx.x; i < rows_out * DK / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(codes)[i];
+  }
+
+  // V: per-channel scale to e4m3, transposed into [D][keys]
+  load_tile<D, T>(v + (int64_t)b * sv.b + (int64_t)s0 * sv.s + (int64_t)h * sv.h, sv.s, valid, tile, PITCH);
+  __syncthreads();
+  {
+    const T* row = reinterpret_cast<const T*>(tile + r * PITCH);
+#pragma unroll 4
+    for (int c = 0; c < D; c += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(row + c);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int kx = 0; kx < 8; kx += 2) {
+        float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
+        float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
+        const uint16_t pk = pack_e4m3x2(y0, y1);
+        vt[(c + kx) * kRows + r] = (uint8_t)(pk & 0xff);
+        vt[(c + kx + 1) * kRows + r] = (uint8_t)(pk >> 8);
+      }
+    }
+  }
+  __syncthreads();
+  {
+    const int chunks = rows_out / 16;  // 16-byte chunks per channel row
+    for (int i = threadIdx.x; i < D * chunks; i += blockDim.x) {
+      const int c = i / chunks;
+      const int q = i - c * chunks;
+      *reinterpret_cast<uint4*>(v8t + ((int64_t)bh * D + c) * spad + s0 + q * 16) =
+          *reinterpret_cast<const uint4*>(vt + c * kRows + q * 16);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// V channel amax (vs must be zero on entry; max via the order of non-negative float bit patterns)
+// ------------------------------------------------------------------------------------------------
+template <int D, typename T>
+__global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, int S, int H, Strides3 st,
+                                                     int rows_per_cta, float* __restrict__ vs) {
+  constexpr int G = D / 8;           // 8-channel groups per row
+  constexpr int RSTEP = 256 / G;     // rows covered per pass
+  __shared__ float red[256][8];
+  const int bh = blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int g = threadIdx.x % G;
+  const int r0 = threadIdx.x / G;
+  const int s_begin = blockIdx.x * rows_per_cta;
+  const int s_end = min(S, s_begin + rows_per_cta);
+  float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (r0 < RSTEP) {
+    const T* base = v + (int64_t)b * st.b + (int64_t)h * st.h + g * 8;
+    for (int s = s_begin + r0; s < s_end; s += RSTEP) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)s * st.s));
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m[k] = fmaxf(m[k], fabsf(to_f32<T>(e[k])));
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) red[threadIdx.x][k] = m[k];
+  __syncthreads();
+  if (threadIdx.x < G) {
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = red[threadIdx.x][k];
+    for (int rr = 1; rr < RSTEP; ++rr)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = fmaxf(acc[k], red[rr * G + threadIdx.x][k]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      atomicMax(reinterpret_cast<unsigned int*>(vs + (int64_t)bh * D + threadIdx.x * 8 + k), __float_as_uint(acc[k]));
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host launchers
+// ------------------------------------------------------------------------------------------------
+template <int D>
+constexpr int q_smem() {
+  return kRows * tile_pitch<D>() + kRows * (D == 64 ? 64 : (D == 256 ? 256 : 128));
+}
+template <int D>
+constexpr int kv_smem() {
+  return q_smem<D>() + D * kRows + D * 4;
+}
+
+static int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s launch: %s", what, cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  return kStatusOk;
+}
+
+template <int D, typename T>
+static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold, int8_t* q8, float* qs,
+                     cudaStream_t stream) {
+  auto kern = quant_q_kernel<D, T>;
+  constexpr int smem = q_smem<D>();
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((S + kRows - 1) / kRows, B * H);
+  kern<<<grid, kRows, smem, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs);
+  return check_launch("quant_q");
+}
+
+template <int D, typename T>
+static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
+                      int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream) {
+  auto kern = quant_kv_kernel<D, T>;
+  constexpr int smem = kv_smem<D>();
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  const int spad = (int)kv_pad(S);
+  dim3 grid((spad + kRows - 1) / kRows, B * H);
+  kern<<<grid, kRows, smem, stream>>>(reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), S, H, sk, sv, vs,
+                                      k8, ks, v8t);
+  return check_launch("quant_kv");
+}
+
+template <int D, typename T>
+static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, cudaStream_t stream) {
+  cudaError_t e = cudaMemsetAsync(vs, 0, sizeof(float) * (size_t)B * H * D, stream);
+  if (e != cudaSuccess) {
+    set_error("v_amax memset: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  // enough CTAs to fill the GPU several times over, each covering a contiguous run of rows
+  const int bh = B * H;
+  int chunks = (S + 511) / 512;
+  const int want = (148 * 8 + bh - 1) / bh;
+  if (chunks > want) chunks = want;
+  if (chunks < 1) chunks = 1;
+  const int rows_per_cta = (S + chunks - 1) / chunks;
+  dim3 grid(chunks, bh);
+  v_amax_kernel<D, T><<<grid, 256, 0, stream>>>(reinterpret_cast<const T*>(v), S, H, st, rows_per_cta, vs);
+  return check_launch("v_amax");
+}
+
+#define SAGE_DISPATCH_D(D_, FN, ...)                                                              \
+  switch (D_) {                                                                                   \
+    case 64: return dtype == 1 ? FN<64, __half>(__VA_ARGS__) : FN<64, __nv_bfloat16>(__VA_ARGS__);     \
+    case 96: return dtype == 1 ? FN<96, __half>(__VA_ARGS__) : FN<96, __nv_bfloat16>(__VA_ARGS__);     \
+    case 128: return dtype == 1 ? FN<128, __half>(__VA_ARGS__) : FN<128, __nv_bfloat16>(__VA_ARGS__);  \
+    case 256: return dtype == 1 ? FN<256, __half>(__VA_ARGS__) : FN<256, __nv_bfloat16>(__VA_ARGS__);  \
+    default: set_error("head_dim %d is not supported (64, 96, 128, 256)", D_); return kStatusUnsupported; \
+  }
+
+int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream) {
+  SAGE_DISPATCH_D(D, v_amax_t, v, B, S, H, st, vs, stream)
+}
+
+int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides3 st, float fold, int8_t* q8,
+                   float* qs, cudaStream_t stream) {
+  SAGE_DISPATCH_D(D, quant_q_t, q, B, S, H, st, fold, q8, qs, stream)
+}
+
+int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
+                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream) {
+  SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream)
+}
+
+}  // namespace sage

@@ -1,0 +1,134 @@
+"""int8 QK / fp8 PV attention on B200: quantise Q, K, V and run the sm_100a kernels.
+
+Host pipeline mirroring src/rdna4_sage/_attention.py of the reference (support checks :70-94, stride
+normalisation :59-67, the quantise + attention launches :97-140), with the kernel launches replaced by
+one call into the C-ABI library (libsage_b200.so): V channel amax, Q quantiser, K+V quantiser and the
+tcgen05 attention kernel, all on torch's current stream, buffers allocated by torch.
+"""
+from __future__ import annotations
+
+import math
+import os
+
+import torch
+
+from . import _lib
+
+KV_BLOCK = 32                           # keys per K-scale block (reference manifest kv_block)
+HEAD_DIMS = (64, 96, 128, 256)
+ARCHS = ("sm_100",)                     # compute capability 10.0: B200 / GB200
+DTYPES = {torch.bfloat16: 0, torch.float16: 1}
+_I32_MAX = 2**31 - 1
+_CHECK = os.environ.get("RDNA4_SAGE_CHECK", "0") not in ("", "0")
+
+_arch_cache: dict[int, str] = {}
+_status: dict[int, torch.Tensor] = {}
+
+
+class Unsupported(Exception):
+    """The inputs fall outside what the packaged kernels handle; use another attention backend."""
+
+
+def device_arch(device: torch.device) -> str:
+    """"sm_XY" of the device's compute capability (the reference reports the gfx arch name)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _arch_cache:
+        major, minor = torch.cuda.get_device_capability(idx)
+        _arch_cache[idx] = f"sm_{major}{minor}"
+    return _arch_cache[idx]
+
+
+def _bsh(t: torch.Tensor, layout: str):
+    """(batch, seq, head) element strides; the kernels need a 16-byte aligned base and strides
+    (8 elements of a 16-bit type), otherwise the tensor is made contiguous.  Reference :59-67."""
+    if t.stride(-1) != 1 or t.data_ptr() % 16:
+        t = t.contiguous()
+    st = (t.stride(0), t.stride(2), t.stride(1)) if layout == "HND" else (t.stride(0), t.stride(1), t.stride(2))
+    if any(s % 8 for s in st):
+        t = t.contiguous()
+        st = (t.stride(0), t.stride(2), t.stride(1)) if layout == "HND" else (t.stride(0), t.stride(1), t.stride(2))
+    return t, st
+
+
+def check_supported(q, k, v, layout, is_causal=False):
+    """Raise Unsupported with the reason if the kernels cannot run these inputs (reference :70-94)."""
+    if layout not in ("HND", "NHD"):
+        raise Unsupported(f"layout {layout!r}")
+    if not (q.is_cuda and k.device == q.device and v.device == q.device):
+        raise Unsupported("tensors must be on one CUDA GPU")
+    if q.dtype not in DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise Unsupported(f"dtype {q.dtype}/{k.dtype}/{v.dtype} (fp16 or bf16 required)")
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise Unsupported("4D tensors required")
+    arch = device_arch(q.device)
+    if arch not in ARCHS:
+        raise Unsupported(f"GPU {arch} is not sm_100 (kernels built for {', '.join(ARCHS)} only)")
+    hd = q.shape[-1]
+    if hd not in HEAD_DIMS or k.shape[-1] != hd or v.shape[-1] != hd:
+        raise Unsupported(f"head_dim {hd} (supported {HEAD_DIMS})")
+    h_ax, s_ax = (1, 2) if layout == "HND" else (2, 1)
+    if q.shape[0] != k.shape[0] or k.shape[0] != v.shape[0] or k.shape[h_ax] != v.shape[h_ax] or \
+            k.shape[s_ax] != v.shape[s_ax]:
+        raise Unsupported("q/k/v batch, k/v heads and k/v lengths must match")
+    if q.shape[h_ax] % k.shape[h_ax]:
+        raise Unsupported(f"heads {q.shape[h_ax]} not a multiple of kv heads {k.shape[h_ax]}")
+    if max(q.numel(), k.numel()) > _I32_MAX or k.shape[s_ax] == 0 or q.shape[s_ax] == 0:
+        raise Unsupported("tensor too large for 32-bit indexing or empty")
+    if is_causal and q.shape[s_ax] != k.shape[s_ax]:
+        raise Unsupported("causal attention needs q_len == kv_len")
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels set to a nonzero SAGE_* code if a bounded wait expires."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _status.get(idx)
+    if w is None:
+        w = _status[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+    return w
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Synchronise and raise RuntimeError if a kernel on `device` reported an error since the last check."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    w = status_word(dev)
+    with torch.cuda.device(dev):
+        rc = _lib.lib().sage_status_sync(w.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(rc, "kernel status")
+
+
+def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=False):
+    """Attention without mask, optionally causal (q_len == kv_len). q: (B, H, Sq, D) for "HND" or (B, Sq, H, D)
+    for "NHD"; k/v alike, with H a multiple of the kv head count. Returns (B, Sq, H, D) contiguous in q's dtype,
+    and with return_lse also the (B, H, Sq) fp32 log-sum-exp of the scaled logits."""
+    check_supported(q, k, v, layout, is_causal)
+    L = _lib.lib()
+    dev = q.device
+    if layout == "HND":
+        B, H, Sq, D = q.shape
+        Hkv, Skv = k.shape[1], k.shape[2]
+    else:
+        B, Sq, H, D = q.shape
+        Skv, Hkv = k.shape[1], k.shape[2]
+    q, sq_ = _bsh(q, layout)
+    k, sk_ = _bsh(k, layout)
+    v, sv_ = _bsh(v, layout)
+    out = torch.empty((B, Sq, H, D), device=dev, dtype=q.dtype)
+    lse = torch.empty((B, H, Sq), device=dev, dtype=torch.float32) if return_lse else None
+    ws_bytes = L.sage_workspace_bytes(B, H, Hkv, Sq, Skv, D)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = L.sage_attention(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[q.dtype], B, H, Hkv, Sq, Skv, D,
+                          *sq_, *sk_, *sv_, float(sm_scale or 0.0), int(bool(is_causal)), out.data_ptr(),
+                          out.stride(0), out.stride(1), out.stride(2), lse.data_ptr() if lse is not None else None,
+                          ws.data_ptr(), ws_bytes, status_word(dev).data_ptr(), stream)
+    _lib.check(rc, "sage_attention")
+    if _CHECK:
+        check_status(dev)
+    return (out, lse) if return_lse else out
+
+
+def sm_fold(sm_scale, head_dim):
+    """Factor folded into the Q scales for a non-default sm_scale (reference :130-131), 1.0 otherwise."""
+    if sm_scale is None or sm_scale <= 0 or math.isclose(sm_scale, head_dim ** -0.5, rel_tol=1e-6):
+        return 1.0
+    return sm_scale * math.sqrt(head_dim)

@@ -1,0 +1,62 @@
+"""The C-ABI library (include/sage_b200.h) loads on a CPU-only host and exports every declared symbol;
+host-side argument checks answer without touching a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from rdna4_sage import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "sage_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sage_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_is_built_in_tree():
+    assert os.path.exists(_lib.LIB_PATH), "run rdna4-sageattention_b200/build_ext.py"
+
+
+def test_exports_every_declared_symbol():
+    syms = declared_symbols()
+    assert {"sage_attention", "sage_attn_fwd", "sage_quant_q", "sage_quant_kv", "sage_v_amax"} <= set(syms)
+    handle = ctypes.CDLL(_lib.LIB_PATH)
+    for s in syms:
+        assert hasattr(handle, s), s
+    # the Python binding declares a signature for every exported entry point
+    assert set(syms) == set(_lib.SIGNATURES), set(syms) ^ set(_lib.SIGNATURES)
+
+
+def test_host_only_queries():
+    L = _lib.lib()
+    assert L.sage_abi_version() == _lib.ABI_VERSION
+    assert [L.sage_qk_row_bytes(d) for d in (64, 96, 128, 256, 80)] == [64, 128, 128, 256, 0]
+    # workspace = q8 + qs + k8 + ks + v8t + vs, each part 256-byte aligned
+    B, H, Hkv, Sq, Skv, D = 1, 40, 40, 32760, 32760, 128
+    sp = 32768
+    parts = [B * H * Sq * 128, B * H * Sq * 4, B * Hkv * sp * 128, B * Hkv * sp // 32 * 4, B * Hkv * D * sp,
+             B * Hkv * D * 4]
+    assert L.sage_workspace_bytes(B, H, Hkv, Sq, Skv, D) == sum((p + 255) // 256 * 256 for p in parts)
+    assert L.sage_workspace_bytes(1, 2, 2, 10, 10, 80) == 0
+
+
+def test_argument_errors_without_gpu():
+    L = _lib.lib()
+    rc = L.sage_attention(None, None, None, 0, 1, 2, 2, 64, 64, 80, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0, None, 0, 0,
+                          0, None, None, 0, None, None)
+    assert rc == _lib.SAGE_ERR_UNSUPPORTED
+    assert b"head_dim 80" in L.sage_last_error()
+    rc = L.sage_attention(None, None, None, 0, 1, 2, 2, 64, 64, 128, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0, None, 0, 0,
+                          0, None, None, 0, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"workspace" in L.sage_last_error()
+    rc = L.sage_attn_fwd(8, 16, 16, 16, 16, 16, 16, 0, 1, 3, 2, 64, 64, 128, 0, 0, 0, 0, None, None, None)
+    assert rc == _lib.SAGE_ERR_UNSUPPORTED      # 3 heads over 2 kv heads
+    rc = L.sage_quant_q(ctypes.c_void_p(8), 0, 1, 64, 2, 128, 8, 8, 8, 1.0, 16, 16, None)
+    assert rc == _lib.SAGE_ERR_INVALID          # misaligned input pointer
+    with pytest.raises(RuntimeError, match="invalid argument"):
+        _lib.check(rc, "sage_quant_q")

@@ -1,0 +1,158 @@
+"""Attention kernel parity on the GPU.
+
+1. Kernel only: the oracle's quantised tensors go through sage_attn_fwd and the output is compared with
+   the oracle's emulation of the same schedule (128-key tiles, per-32-key lazy max) and of the
+   reference's schedule (32-key tiles).
+2. Full path: torch.ops.rdna4_sage.attention (quantisers + kernel) against the emulation of the
+   reference's arithmetic (mean relative L1 <= 1e-2) and against fp32 attention (cosine).
+3. The reference's own kernel cases (tests/test_attention.py:11-30 of the reference): cosine > 0.998
+   against fp32 SDPA.
+"""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import rdna4_sage
+from oracle import sage_oracle as O
+from sage_gpu_helpers import (cos, gpu_attn_from_quant, make_qkv, oracle_quant, oracle_to_kernel_layout, rel_l1,
+                              to_bshd_np, TORCH_DT)
+
+pytestmark = pytest.mark.gpu
+
+REL_L1_REFERENCE = 1e-2     # vs the emulation of the reference's 32-key schedule
+REL_L1_SCHEDULE = 2e-3      # vs the emulation of the kernel's own schedule (same fp8 roundings)
+LSE_TOL = 1e-3              # kernel LSE vs emulated LSE (natural log)
+
+
+def _emulate(qn, kn, vn, sm_scale, causal, rows, block_n, out_dtype):
+    q8, qs, k8, ks, v8, vs = oracle_quant(qn, kn, vn, sm_scale)
+    B, Sq, H, D = qn.shape
+    Skv, Hkv = kn.shape[1], kn.shape[2]
+    out = np.zeros((B, len(rows), H, D), np.float32)
+    lse = np.zeros((B, H, len(rows)), np.float32)
+    for b in range(B):
+        for h in range(H):
+            hk = h // (H // Hkv)
+            o, l = O.attention_rows(q8[b, :, h], qs[b, h], k8[b, :, hk], ks[b, hk], v8[b, :, hk], vs[b, hk], rows, Sq,
+                                    Skv, causal, block_n=block_n)
+            out[b, :, h] = O.round_to_dtype(o, out_dtype)
+            lse[b, h] = l
+    return out, lse
+
+
+KERNEL_CASES = [  # B, H, Hkv, Sq, Skv, D, causal, dist
+    (1, 2, 2, 256, 256, 128, False, "normal"),
+    (2, 4, 2, 300, 517, 128, False, "flux"),
+    (1, 2, 1, 200, 200, 64, True, "normal"),
+    (1, 3, 3, 333, 129, 96, False, "offset1"),
+    (1, 2, 2, 257, 257, 256, True, "offset2"),
+    (1, 2, 2, 130, 1000, 256, False, "flux"),
+    (1, 4, 4, 640, 640, 128, True, "flux"),
+]
+
+
+@pytest.mark.parametrize("case", KERNEL_CASES)
+@pytest.mark.parametrize("out_dtype", ["bf16", "f16"])
+def test_kernel_only_matches_emulation(case, out_dtype):
+    B, H, Hkv, Sq, Skv, D, causal, dist = case
+    q, k, v = make_qkv(sum(case[:6]), B, H, Hkv, Sq, Skv, D, "NHD", out_dtype, dist=dist, device="cpu")
+    qn, kn, vn = (t.float().numpy() for t in (q, k, v))
+    quant = oracle_quant(qn, kn, vn)
+    qt = oracle_to_kernel_layout(*quant, "cuda")
+    qt.update(B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D)
+    out, lse = gpu_attn_from_quant(qt, TORCH_DT[out_dtype], causal, with_lse=True)
+    rows = np.arange(Sq)
+    emu128, lse128 = _emulate(qn, kn, vn, None, causal, rows, 128, out_dtype)
+    emu32, _ = _emulate(qn, kn, vn, None, causal, rows, 32, out_dtype)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_l1(got, emu128) < REL_L1_SCHEDULE, rel_l1(got, emu128)
+    assert rel_l1(got, emu32) < REL_L1_REFERENCE, rel_l1(got, emu32)
+    np.testing.assert_allclose(lse.cpu().numpy(), lse128, atol=LSE_TOL, rtol=0)
+
+
+def _fp32_ref(q, k, v, layout, causal, scale=None):
+    th = (lambda t: t) if layout == "HND" else (lambda t: t.transpose(1, 2))
+    rep = th(q).shape[1] // th(k).shape[1]
+    o = F.scaled_dot_product_attention(th(q).float(), th(k).float().repeat_interleave(rep, 1),
+                                       th(v).float().repeat_interleave(rep, 1), is_causal=causal, scale=scale)
+    return th(o)
+
+
+FULL_CASES = [  # B, H, Hkv, Sq, Skv, D, layout, dtype, causal, dist, sm_scale
+    (1, 4, 4, 1024, 1024, 128, "HND", "bf16", False, "flux", None),
+    (1, 4, 2, 777, 1031, 128, "NHD", "f16", False, "offset2", 0.05),
+    (2, 2, 2, 1000, 1000, 64, "NHD", "bf16", True, "varlen", None),
+    (1, 3, 1, 600, 900, 96, "HND", "bf16", False, "normal", None),
+    (1, 2, 2, 700, 700, 256, "NHD", "f16", True, "offset1", None),
+]
+
+
+@pytest.mark.parametrize("case", FULL_CASES)
+def test_full_path_matches_emulation_and_fp32(case):
+    B, H, Hkv, Sq, Skv, D, layout, dtype, causal, dist, sm_scale = case
+    q, k, v = make_qkv(sum(case[:6]), B, H, Hkv, Sq, Skv, D, layout, dtype, dist=dist)
+    out = rdna4_sage.attention(q, k, v, layout, sm_scale=sm_scale, is_causal=causal)
+    assert out.dtype == q.dtype and out.shape == q.shape
+    rdna4_sage._attention.check_status(q.device)
+    ref = _fp32_ref(q, k, v, layout, causal, sm_scale)
+    c = cos(out.float().cpu(), ref.cpu())
+    assert c > (0.998 if dist == "flux" else 0.999), c
+    rows = np.unique(np.linspace(0, Sq - 1, 96).astype(np.int64))
+    emu, _ = _emulate(*(to_bshd_np(t, layout) for t in (q, k, v)), sm_scale, causal, rows, 32, dtype)
+    got = to_bshd_np(out, layout)[:, rows]
+    assert rel_l1(got, emu) < REL_L1_REFERENCE, rel_l1(got, emu)
+
+
+REFERENCE_CASES = [  # reference tests/test_attention.py:11-30: name, B, Sq, Skv, H, Hkv, D, layout, dtype[, causal]
+    ("SDXL self", 2, 4096, 4096, 10, 10, 64, "NHD", "f16"),
+    ("SD3.5 joint", 1, 4250, 4250, 24, 24, 64, "NHD", "f16"),
+    ("Flux joint", 1, 4352, 4352, 24, 24, 128, "HND", "bf16"),
+    ("Flux.2 joint", 1, 4608, 4608, 48, 48, 128, "HND", "bf16"),
+    ("Qwen-Image 1328", 1, 6889, 6889, 24, 24, 128, "HND", "bf16"),
+    ("Neta Lumina", 1, 4352, 4352, 24, 24, 96, "HND", "bf16"),
+    ("Lumina GQA 24/8", 1, 4096, 4096, 24, 8, 96, "HND", "bf16"),
+    ("Wan 1.3B 480p", 1, 32760, 32760, 12, 12, 128, "NHD", "f16"),
+    ("Wan cross 512", 1, 32760, 512, 12, 12, 128, "NHD", "f16"),
+    ("LTXV 2B", 1, 4992, 4992, 32, 32, 64, "NHD", "bf16"),
+    ("odd lengths", 3, 777, 1031, 6, 6, 128, "HND", "f16"),
+    ("AuraFlow joint d256", 1, 4360, 4360, 12, 12, 256, "HND", "f16"),
+    ("d256 odd lengths", 2, 777, 1031, 4, 4, 256, "NHD", "bf16"),
+    ("causal d128", 1, 4096, 4096, 24, 24, 128, "HND", "bf16", True),
+    ("causal d64 odd", 2, 1000, 1000, 8, 8, 64, "NHD", "f16", True),
+    ("causal d96 GQA 24/8", 1, 2048, 2048, 24, 8, 96, "HND", "bf16", True),
+    ("causal d256", 1, 3000, 3000, 8, 8, 256, "NHD", "f16", True),
+    ("causal d128 long", 1, 16384, 16384, 12, 12, 128, "HND", "bf16", True),
+]
+
+
+@pytest.mark.parametrize("case", REFERENCE_CASES, ids=[c[0] for c in REFERENCE_CASES])
+def test_reference_kernel_cases(case):
+    name, B, Sq, Skv, H, Hkv, D, layout, dtype, *causal = case
+    causal = bool(causal and causal[0])
+    g = torch.Generator(device="cuda").manual_seed(0)
+    dt = TORCH_DT[dtype]
+    shape = (lambda s, h: (B, h, s, D)) if layout == "HND" else (lambda s, h: (B, s, h, D))
+    q = torch.randn(shape(Sq, H), device="cuda", dtype=dt, generator=g)
+    k = torch.randn(shape(Skv, Hkv), device="cuda", dtype=dt, generator=g)
+    v = torch.randn(shape(Skv, Hkv), device="cuda", dtype=dt, generator=g)
+    out = rdna4_sage.attention(q, k, v, tensor_layout=layout, is_causal=causal)
+    assert out.dtype == dt and out.shape == q.shape
+    ref = _fp32_ref(q, k, v, layout, causal)
+    c = cos(out.float(), ref)
+    assert c > 0.998, (name, c)
+    rdna4_sage._attention.check_status(q.device)
+
+
+def test_lse_against_exact_logsumexp():
+    q, k, v = make_qkv(5, 1, 4, 4, 2048, 2048, 128, "HND", "bf16")
+    for causal in (False, True):
+        out, lse = torch.ops.rdna4_sage.attention_lse(q, k, v, "HND", 0.0, causal)
+        sc = q.float() @ k.float().transpose(-1, -2) * 128 ** -0.5
+        if causal:
+            sc.masked_fill_(torch.ones(2048, 2048, dtype=torch.bool, device="cuda").triu(1), float("-inf"))
+        exact = torch.logsumexp(sc, -1)
+        err = (lse - exact).abs()
+        assert lse.shape == (1, 4, 2048) and lse.dtype == torch.float32
+        assert float(err.max()) < 2e-2 and float(err.mean()) < 2e-3, (float(err.max()), float(err.mean()))

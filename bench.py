@@ -169,6 +169,32 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
+    """Time the public API with pinned host inputs copied in and the output copied out every step."""
+    import sageattention
+
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        o = sageattention.sageattn(dq, dk, dv, tensor_layout="NHD")
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    n = max(2, args.steps // 2)
+    e0.record(stream)
+    for _ in range(n):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return max_over_ranks(e0.elapsed_time(e1) / n), h2d, d2h
+
+
 def run_ours(args):
     import rdna4_sage
     import sageattention
@@ -185,11 +211,11 @@ def run_ours(args):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    heads = H
+    heads = args.heads
     if args.strong and world > 1:
-        heads = H // world + (1 if rank < H % world else 0)
-    q, k, v = make_inputs(dev, h=heads, seed=rank)
-    ops = ops_per_call(h=heads)
+        heads = args.heads // world + (1 if rank < args.heads % world else 0)
+    q, k, v = make_inputs(dev, h=heads, n=args.seq, seed=rank)
+    ops = ops_per_call(h=heads, n=args.seq)
     stream = torch.cuda.current_stream(dev)
 
     def step():
@@ -224,30 +250,13 @@ def run_ours(args):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     barrier()
     rdna4_sage._attention.check_status(dev)
-    total_ops = ops_per_call() if args.strong else ops * world
+    total_ops = ops_per_call(h=args.heads, n=args.seq) if args.strong else ops * world
     value = total_ops / (ms * 1e-3) / 1e12
 
     # ---- e2e: public API with pinned host buffers, copies inside every step
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
-    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
-    d2h = hout.numel() * hout.element_size()
-
-    def e2e_step():
-        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
-        o = sageattention.sageattn(dq, dk, dv, tensor_layout="NHD")
-        hout.copy_(o, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    e0.record(stream)
-    for _ in range(max(2, args.steps // 2)):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / max(2, args.steps // 2))
-    del hq, hk, hv, hout
+    ms_e2e, h2d, d2h = None, 0, 0
+    if not args.no_e2e:
+        ms_e2e, h2d, d2h = run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks)
 
     # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream)
     L = _lib.lib()
@@ -328,8 +337,9 @@ def run_ours(args):
                                        f"dp{world}: one call's (batch, head) units per rank, no collective"),
                        "l2": "inputs 1.0 GB per rank > 126 MB L2 (no flush needed)"},
             "clocks": clocks.summary(),
-            "e2e": {"value": total_ops / (ms_e2e * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms_e2e,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": None if ms_e2e is None else
+            {"value": total_ops / (ms_e2e * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms_e2e,
+             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
                          "frac": achieved / peak_tops, "traffic": traffic,
@@ -357,6 +367,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--strong", action="store_true", help="split the heads of one call across ranks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-copy leg")
+    ap.add_argument("--heads", type=int, default=H, help="heads per call (profiling: a smaller case)")
+    ap.add_argument("--seq", type=int, default=N, help="tokens per call (profiling: a smaller case)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -59,9 +59,23 @@ struct AttnCfg {
   static constexpr int K_TILE = BN * DK;
   static constexpr int V_TILE = D * BN;
   static constexpr int NST = D == 64 ? 6 : (D == 256 ? 2 : 4);
-  static constexpr int THREADS = 128 * QT + 64;
+#ifndef SAGE_NO_SETMAXNREG
+  // QT = 2: three full warpgroups (softmax 0, softmax 1, producer + MMA + two idle warps) so the
+  // register file can be rebalanced towards the softmax warpgroups with setmaxnreg.
+  static constexpr bool REBALANCE = QT == 2;
+#else
+  static constexpr bool REBALANCE = false;
+#endif
+  static constexpr int THREADS = REBALANCE ? 384 : 128 * QT + 64;
   static constexpr int PRODUCER_WARP = 4 * QT;
   static constexpr int MMA_WARP = 4 * QT + 1;
+  // registers per thread at launch (the launch bound gives 65536 / 384 rounded down to 8) and after
+  // the rebalance; the shares must add up to exactly what the CTA was launched with
+  static constexpr int REGS_LAUNCH = 168;
+  static constexpr int REGS_SOFTMAX = 200;
+  static constexpr int REGS_OTHER = 104;
+  static_assert(!REBALANCE || 2 * 128 * REGS_SOFTMAX + 128 * REGS_OTHER == THREADS * REGS_LAUNCH,
+                "setmaxnreg shares must sum to the launch allocation");
   static constexpr int O_COL = 256;
   static constexpr int TMEM_COLS = 512;
   static constexpr int NUM_BARS = 1 + 3 * NST + 2 + 2 + 2 + 1;
@@ -72,6 +86,70 @@ struct AttnCfg {
 
 __device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) {
   return (uint32_t)pack_e4m3x2(a, b) | ((uint32_t)pack_e4m3x2(c, d) << 16);
+}
+
+// One query row's share of a 128-key tile: the lazy max update over the four 32-key blocks, then
+// p = exp2(s * c * ks_b - c * m_new) for all 128 keys, packed to e4m3 (4 keys per word, key 4w+b in
+// byte b) and summed in fp32.  MASK: keys >= lim are excluded (edge tiles only).  Returns the sum of p
+// and the new running max in m_new (the caller derives the correction factor).
+template <bool MASK>
+__device__ __forceinline__ float softmax_tile(uint32_t (&s)[4][32], const float (&ksv)[4], float c, float m,
+                                              int kv0, int lim, float& m_new, uint32_t (&pw)[32]) {
+  if (MASK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
+  }
+  // lazy running max, decided per 32-key block in key order as the reference's 32-key tiles do
+  m_new = m;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int mx = max32_tree(s[i]);
+    if (!MASK || mx != INT32_MIN) {
+      const float cand = fmaxf(m_new, (float)mx * ksv[i]);
+      if (cand != -INFINITY && (cand - m_new) * c > 8.0f) m_new = cand;
+    }
+  }
+  const float negcm = m_new == -INFINITY ? 0.f : -(c * m_new);
+  const uint64_t neg2 = f2_pack(negcm, negcm);
+  const uint64_t unbias2 = f2_pack(-kMagicF, -kMagicF);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float cts = c * ksv[i];
+    const uint64_t cts2 = f2_pack(cts, cts);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      float pv[4];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int e = w * 4 + hh * 2;
+        // exact int32 -> fp32 (|s| < 2^22), then fma(s, c*ks, -c*m) on both lanes
+        uint64_t x = f2_pack(__int_as_float((int)s[i][e] + kMagicI), __int_as_float((int)s[i][e + 1] + kMagicI));
+        x = f2_add(x, unbias2);
+        float y0, y1;
+        f2_unpack(f2_fma(x, cts2, neg2), y0, y1);
+        float p0 = fast_exp2(y0);
+        float p1 = fast_exp2(y1);
+        if (MASK) {
+          if ((int)s[i][e] == INT32_MIN) p0 = 0.f;
+          if ((int)s[i][e + 1] == INT32_MIN) p1 = 0.f;
+        }
+        pv[hh * 2] = p0;
+        pv[hh * 2 + 1] = p1;
+        acc[(w * 2 + hh) & 3] = f2_add(acc[(w * 2 + hh) & 3], f2_pack(p0, p1));
+      }
+      pw[i * 8 + w] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
+    }
+  }
+  float a0, a1, a2, a3, a4, a5, a6, a7;
+  f2_unpack(acc[0], a0, a1);
+  f2_unpack(acc[1], a2, a3);
+  f2_unpack(acc[2], a4, a5);
+  f2_unpack(acc[3], a6, a7);
+  return ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
 }
 
 template <int D, bool CAUSAL>
@@ -138,7 +216,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const WaitCtx wc{cta_abort, p.status};
-
+  if (warp >= 4 * QT) {
+    // warpgroup of the producer and MMA warps (plus idle warps when THREADS = 384)
+    if constexpr (C::REBALANCE) regs_decrease<C::REGS_OTHER>();
   if (warp == C::PRODUCER_WARP) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0 && n_tiles > 0) {
@@ -246,8 +326,10 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       tc_commit(mma_drain);
       mbar_drain(mma_drain, 0);
     }
+  }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
+    if constexpr (C::REBALANCE) regs_increase<C::REGS_SOFTMAX>();
     const int t = warp >> 2;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
@@ -260,6 +342,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
+    float ksn[4];  // K scales of the next tile, loaded one iteration ahead
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ksn[i] = i < p.nkb ? __ldg(ksb + i) : 0.f;
     for (int j = 0; j < n_tiles; ++j) {
       const int slot = QT == 2 ? t : (j & 1);
       const uint32_t sph = QT == 2 ? (j & 1) : ((j >> 1) & 1);
@@ -267,8 +352,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       float ksv[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int kb = j * 4 + i;
-        ksv[i] = kb < p.nkb ? __ldg(ksb + kb) : 0.f;
+        ksv[i] = ksn[i];
+        const int kb = (j + 1) * 4 + i;
+        ksn[i] = kb < p.nkb ? __ldg(ksb + kb) : 0.f;
       }
       if (!mbar_wait(&s_full[slot], sph, wc)) {
         ok = false;
@@ -281,48 +367,15 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       tmem_wait_ld();
       const bool need_mask = (kv0 + C::BN > p.Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
       const int lim = min(p.Skv, CAUSAL ? last_key + 1 : p.Skv);  // keys < lim are kept
-      // Lazy running max, decided per 32-key block in key order exactly as the reference's 32-key
-      // tiles do: the max moves only when a block's scaled max exceeds it by more than 8 / c.
-      float m_new = m;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        int mx = INT32_MIN;
-        if (need_mask) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (kv0 + i * 32 + e < lim) mx = max(mx, (int)s[i][e]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mx = max(mx, (int)s[i][e]);
-        }
-        if (mx != INT32_MIN || !need_mask) {
-          const float cand = fmaxf(m_new, (float)mx * ksv[i]);
-          if (cand != -INFINITY && (cand - m_new) * c > 8.0f) m_new = cand;
-        }
-      }
+      uint32_t pw[32];
+      float sum;
+      float m_new;
+      if (need_mask)
+        sum = softmax_tile<true>(s, ksv, c, m, kv0, lim, m_new, pw);
+      else
+        sum = softmax_tile<false>(s, ksv, c, m, kv0, lim, m_new, pw);
       const bool need = m_new != m;
       const float corr = need ? fast_exp2((m - m_new) * c) : 1.0f;
-      const float negcm = m_new == -INFINITY ? 0.f : -(c * m_new);
-      float sum = 0.f;
-      uint32_t pw[32];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float cts = c * ksv[i];
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-          float pv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int idx = w * 4 + e;
-            const float sf = __int_as_float((int)s[i][idx] + kMagicI) - kMagicF;
-            float x = fast_exp2(fmaf(sf, cts, negcm));
-            if (need_mask && kv0 + i * 32 + idx >= lim) x = 0.f;
-            pv[e] = x;
-            sum += x;
-          }
-          pw[i * 8 + w] = pack_p4(pv[0], pv[1], pv[2], pv[3]);
-        }
-      }
       l = corr * l + sum;
       tmem_st32(tl + slot * 128, pw);
       if (__any_sync(0xffffffffu, need && j > 0)) {

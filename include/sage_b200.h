@@ -89,6 +89,19 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
                    int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb, int64_t oss,
                    int64_t osh, float* lse, void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/* sage_attention without a workspace argument, for callers that cannot allocate device memory (a host
+ * framework that owns all device memory through its own pool, or an FFI caller with no CUDA allocator):
+ * the quantised tensors live in a 32 MiB array inside the library, held by every GPU that loads it.
+ * This entry point has no counterpart in the reference (whose Python host always allocates through
+ * torch).  Calls needing more than 32 MiB of scratch (sage_workspace_bytes) return SAGE_ERR_UNSUPPORTED.
+ * All calls share the array, so calls that overlap on the GPU race; order them on one stream.  The
+ * first call on a device looks up the array's address with cudaGetSymbolAddress: make it before any
+ * stream capture. */
+int sage_attention_static(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
+                          int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss,
+                          int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out,
+                          int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream);
+
 /* Synchronise `stream`, read and clear a status word (NULL = the library's own word on the current
  * device); returns the code it held (SAGE_OK when no kernel reported an error). */
 int sage_status_sync(int* status, void* stream);

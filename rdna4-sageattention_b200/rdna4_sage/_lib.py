@@ -45,6 +45,9 @@ SIGNATURES = {
     "sage_attention": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64,
                               _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p, _c_i64, _c_i64,
                               _c_i64, _c_p, _c_p, _c_sz, _c_p, _c_p]),
+    "sage_attention_static": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,
+                                     _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,
+                                     _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
     "sage_status_sync": (_c_i, [_c_p, _c_p]),
 }
 ABI_VERSION = 1

@@ -311,11 +311,14 @@ def run_ours(args):
     peaks, peak_kind = load_peaks()
     peak_tops = 2.0 * peaks["bf16_tflops_sustained"]
     achieved = ops / (attn_ms * 1e-3) / 1e12
+    # DRAM traffic of one full launch from the committed ncu summary (measured on a smaller case and
+    # scaled by units processed, as that file states); None when absent or for other shapes
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", "attn_wan_traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
+    tpath = os.path.join(ROOT, "profiles", "attn_wan_d128.md")
+    if os.path.exists(tpath) and (args.heads, args.seq) == (H, N):
+        import re
+        mt = re.search(r"traffic_bytes_per_full_launch:\s*(\d+)", open(tpath).read())
+        traffic = int(mt.group(1)) if mt else None
     elems = Bq * Sq * Hq * Dq
     quant_bytes = 3 * elems * 2 + 3 * elems + (Bq * Hq * Sq + Bq * Hq * spad // 32 + Bq * Hq * Dq) * 4
     quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9

@@ -1,0 +1,143 @@
+"""Context-parallel attention for very long sequences: each rank holds one chunk of the tokens.
+
+Steps per call (all ranks of `group`, same order):
+  1. V channel amax of the local chunk, then an all-reduce (MAX) so every rank quantises V with the same
+     per-channel scale as a single-GPU call would;
+  2. local Q quantisation, local K+V quantisation with the global amax (chunks start at multiples of 32
+     tokens, so every 32-key K scale block lies inside one chunk and equals the single-GPU one);
+  3. all-gather of the quantised K (int8), its block scales and V^T (e4m3) - 1 byte per element instead of
+     the 2-byte inputs - and reassembly into the kernel's [B, Hkv, S, DK] / [B, Hkv, D, S] layouts;
+  4. the attention kernel on the local query rows against all keys.
+The output rows of each rank equal the corresponding rows of the single-GPU call bit for bit.
+
+The collective is NCCL through torch.distributed (one process per GPU).  Causal attention is not
+supported here (a rank's rows would need the global row offset).
+"""
+from __future__ import annotations
+
+
+import torch
+import torch.distributed as dist
+
+from . import _attention, _lib
+
+KV_BLOCK = _attention.KV_BLOCK
+
+
+def chunk_bounds(S: int, world: int, rank: int, align: int = KV_BLOCK) -> tuple[int, int]:
+    """[start, end) of rank's token chunk: equal chunks rounded up to `align`, the last one shorter."""
+    per = (S + world - 1) // world
+    per = (per + align - 1) // align * align
+    start = min(rank * per, S)
+    return start, min(start + per, S)
+
+
+class KernelBackend:
+    """The C-ABI kernels (the product path)."""
+
+    def __init__(self, device):
+        self.L = _lib.lib()
+        self.device = device
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+
+    def qk_row_bytes(self, D):
+        return self.L.sage_qk_row_bytes(D)
+
+    def v_amax(self, v, vs):
+        B, S, H, D = v.shape
+        _lib.check(self.L.sage_v_amax(v.data_ptr(), _attention.DTYPES[v.dtype], B, S, H, D, *v.stride()[:3],
+                                      vs.data_ptr(), self.stream), "sage_v_amax")
+
+    def quant_q(self, q, fold, q8, qs):
+        B, S, H, D = q.shape
+        _lib.check(self.L.sage_quant_q(q.data_ptr(), _attention.DTYPES[q.dtype], B, S, H, D, *q.stride()[:3],
+                                       fold, q8.data_ptr(), qs.data_ptr(), self.stream), "sage_quant_q")
+
+    def quant_kv(self, k, v, vs, k8, ks, v8t):
+        B, S, H, D = k.shape
+        _lib.check(self.L.sage_quant_kv(k.data_ptr(), v.data_ptr(), _attention.DTYPES[k.dtype], B, S, H, D,
+                                        *k.stride()[:3], *v.stride()[:3], vs.data_ptr(), k8.data_ptr(),
+                                        ks.data_ptr(), v8t.data_ptr(), self.stream), "sage_quant_kv")
+
+    def attn(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D):
+        B = out.shape[0]
+        _lib.check(self.L.sage_attn_fwd(q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(),
+                                        vs.data_ptr(), out.data_ptr(), _attention.DTYPES[out.dtype], B, H, Hkv, Sq,
+                                        Skv, D, 0, *out.stride()[:3], None,
+                                        _attention.status_word(out.device).data_ptr(), self.stream), "sage_attn_fwd")
+
+
+def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=None):
+    """Context-parallel attention over `group`.
+
+    q, k, v: this rank's chunk (B, S_r, H, D) / (B, S_r, Hkv, D) in NHD layout, chunk r covering tokens
+    chunk_bounds(total_len, world, r).  Returns this rank's output rows (B, S_r, H, D) in q's dtype.
+    """
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, Sr, H, D = q.shape
+    Hkv = k.shape[2]
+    start, end = chunk_bounds(total_len, world, rank)
+    if end - start != Sr or k.shape[1] != Sr or v.shape[1] != Sr:
+        raise ValueError(f"rank {rank}: expected a chunk of {end - start} tokens, got q {Sr}, k {k.shape[1]}")
+    be = backend if backend is not None else KernelBackend(q.device)
+    dev = q.device
+    per = chunk_bounds(total_len, world, 0)[1]          # padded chunk length (a multiple of 32)
+    dk = be.qk_row_bytes(D)
+    # 1. global V channel amax
+    vs = torch.zeros((B, Hkv, D), device=dev, dtype=torch.float32)
+    be.v_amax(v, vs)
+    dist.all_reduce(vs, op=dist.ReduceOp.MAX, group=group)
+    # 2. local quantisation; every rank's K chunk is quantised to `per` rows (zero rows past its end)
+    fold = float(_attention.sm_fold(sm_scale, D))
+    q8 = torch.empty((B, H, Sr, dk), device=dev, dtype=torch.int8)
+    qs = torch.empty((B, H, Sr), device=dev, dtype=torch.float32)
+    be.quant_q(q, fold, q8, qs)
+    k8 = torch.zeros((B, Hkv, per, dk), device=dev, dtype=torch.int8)
+    ks = torch.zeros((B, Hkv, per // KV_BLOCK), device=dev, dtype=torch.float32)
+    v8t = torch.zeros((B, Hkv, D, per), device=dev, dtype=torch.uint8)
+    if Sr > 0:
+        spad = (Sr + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
+        k8_l = torch.empty((B, Hkv, spad, dk), device=dev, dtype=torch.int8)
+        ks_l = torch.empty((B, Hkv, spad // KV_BLOCK), device=dev, dtype=torch.float32)
+        v8t_l = torch.empty((B, Hkv, D, spad), device=dev, dtype=torch.uint8)
+        be.quant_kv(k, v, vs, k8_l, ks_l, v8t_l)
+        k8[:, :, :spad] = k8_l
+        ks[:, :, :spad // KV_BLOCK] = ks_l
+        v8t[..., :spad] = v8t_l
+    # 3. all-gather the quantised keys and values, then reassemble [B, Hkv, world*per, ...]
+    g_k8 = torch.empty((world,) + tuple(k8.shape), device=dev, dtype=torch.int8)
+    g_ks = torch.empty((world,) + tuple(ks.shape), device=dev, dtype=torch.float32)
+    g_v8 = torch.empty((world,) + tuple(v8t.shape), device=dev, dtype=torch.uint8)
+    dist.all_gather_into_tensor(g_k8, k8, group=group)
+    dist.all_gather_into_tensor(g_ks, ks, group=group)
+    dist.all_gather_into_tensor(g_v8, v8t, group=group)
+    spad_total = world * per
+    k8_full = g_k8.permute(1, 2, 0, 3, 4).reshape(B, Hkv, spad_total, dk)
+    ks_full = g_ks.permute(1, 2, 0, 3).reshape(B, Hkv, spad_total // KV_BLOCK)
+    v8t_full = g_v8.permute(1, 2, 3, 0, 4).reshape(B, Hkv, D, spad_total)
+    # keys past total_len are zero in every chunk; the kernel masks keys >= total_len.  Trim the padded
+    # tail to the single-GPU padded length so the layouts match it exactly.
+    spad_exact = (total_len + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
+    k8_full = k8_full[:, :, :spad_exact].contiguous()
+    ks_full = ks_full[:, :, :spad_exact // KV_BLOCK].contiguous()
+    v8t_full = v8t_full[..., :spad_exact].contiguous()
+    # 4. local rows against all keys
+    out = torch.empty((B, Sr, H, D), device=dev, dtype=q.dtype)
+    if Sr > 0:
+        be.attn(q8, qs, k8_full, ks_full, v8t_full, vs, out, H, Hkv, Sr, total_len, D)
+    return out
+
+
+def shard(x: torch.Tensor, total_len: int, world: int, rank: int, seq_dim: int = 1) -> torch.Tensor:
+    """This rank's chunk of a full (B, S, H, D) tensor (a helper for callers and tests)."""
+    s, e = chunk_bounds(total_len, world, rank)
+    return x.narrow(seq_dim, s, e - s)
+
+
+def ops_per_rank(B, H, Sr, S, D) -> float:
+    """Algorithmic operations of one rank's share (4 * B * H * Sr * S * D)."""
+    return 4.0 * B * H * Sr * S * D
+
+
+__all__ = ["attention_cp", "chunk_bounds", "shard", "KernelBackend", "ops_per_rank"]

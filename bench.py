@@ -125,6 +125,7 @@ def cpu_baseline(seconds_target=12.0):
     """The reference's CPU path (oracle restatement of src/rdna4_sage/__init__.py:44-58) on a head subset."""
     from oracle import sage_oracle as O
 
+    _use_all_host_threads()
     heads = 1
     q, k, v = make_inputs("cpu", h=heads)
     t0 = time.perf_counter()
@@ -142,11 +143,22 @@ def cpu_baseline(seconds_target=12.0):
                       f"(full call ~ {dt * H:.1f} s)"}
 
 
+def _use_all_host_threads():
+    """torchrun sets OMP_NUM_THREADS=1 per process; the CPU leg uses every core this process may run on."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(max(1, n))
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import sage_oracle as O
+
+    _use_all_host_threads()
 
     heads = 1
     q, k, v = make_inputs("cpu", h=heads)
@@ -193,6 +205,67 @@ def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
     e1.record(stream)
     torch.cuda.synchronize()
     return max_over_ranks(e0.elapsed_time(e1) / n), h2d, d2h
+
+
+HUNYUAN = (1, 24, 67576, 128)
+
+
+def run_hunyuan_cp(args):
+    """HunyuanVideo-shaped call (B1 H24 N67576 D128) split by sequence over the ranks (context parallel:
+    NCCL all-reduce of the V amax and all-gather of the quantised K/V).  One call = one step."""
+    import datetime
+
+    import torch.distributed as dist
+
+    import rdna4_sage
+    from rdna4_sage import cp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    b, h, n, d = HUNYUAN
+    q, k, v = make_inputs(dev, b=b, h=h, n=n, d=d, seed=0)
+    if world > 1:
+        q, k, v = (cp.shard(t, n, world, rank).contiguous() for t in (q, k, v))
+
+    def step():
+        if world > 1:
+            return cp.attention_cp(q, k, v, n)
+        return rdna4_sage.attention(q, k, v, "NHD")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = ops_per_call(b, h, n, d) / (ms * 1e-3) / 1e12
+    if rank == 0:
+        print(json.dumps({"metric": "ms/call & TOPS, 67576-tok 24-head d128 sageattn (context parallel)",
+                          "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+                          "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                          "scaling": "strong", "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (bf16 in, bf16 out)",
+                          "data": "synthetic",
+                          "config": {"workload": "hunyuanvideo-544p self-attention call, sequence split over ranks",
+                                     "global_batch": 1, "seq_len": n, "parallelism": f"cp{world}"}}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_ours(args):
@@ -369,6 +442,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--strong", action="store_true", help="split the heads of one call across ranks")
+    ap.add_argument("--workload", choices=["wan", "hunyuan"], default="wan",
+                    help="wan: the metric's call; hunyuan: the >64K call with the sequence split over ranks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-copy leg")
     ap.add_argument("--heads", type=int, default=H, help="heads per call (profiling: a smaller case)")
@@ -378,6 +453,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "hunyuan":
+        run_hunyuan_cp(args)
     else:
         run_ours(args)
 

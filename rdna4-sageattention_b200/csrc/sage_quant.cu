@@ -9,7 +9,8 @@
 //    per-channel max |V|.                                                  (sage_quant.py:51-70)
 // The rotation is a fast Walsh-Hadamard transform in registers (one thread per token row, fp32
 // butterflies); it equals the reference's fp32-accumulated product with Hm up to fp32 summation order.
-// Each CTA stages a 128-row tile through shared memory so global loads and stores are coalesced.
+// One thread per token row: the row's 2*D bytes are contiguous, so each thread streams them with 16-byte
+// loads (every L2 sector it touches is used in full) and writes its code row with 16-byte stores.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -47,40 +48,38 @@ __device__ __forceinline__ void fwht(float* x) {
   }
 }
 
-// trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32.
-__device__ __forceinline__ int quant_code(float x, float scale) {
-  const float y = __fdiv_rn(x, scale);
-  const float t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
+// trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32 (the reference's
+// rounding, kernel_build/sage_quant.py:44,65).  `rcp` is the correctly rounded 1/scale.  x * rcp is within
+// two ulps of the IEEE quotient, so it gives the same code unless y +- 0.5 lies within a few ulps of an
+// integer; those rare elements are recomputed with the IEEE division.
+__device__ __forceinline__ int quant_code(float x, float scale, float rcp) {
+  float y = x * rcp;
+  float t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
+  const float at = fabsf(t);
+  const float fr = at - truncf(at);
+  if (fr < 1e-4f || fr > 1.0f - 1e-4f) {
+    y = __fdiv_rn(x, scale);
+    t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
+  }
   return __float2int_rz(t);
 }
 
-constexpr int kRows = 128;  // token rows per CTA (one per thread)
+constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)
 
-// Cooperative coalesced copy of a [kRows][D] tile (rows strided by `row_stride` elements) into shared
-// memory rows of `pitch` bytes.  Rows >= valid are zero-filled.
-template <int D, typename T>
-__device__ __forceinline__ void load_tile(const T* __restrict__ src, int64_t row_stride, int valid, uint8_t* tile,
-                                          int pitch) {
-  constexpr int kChunks = D * 2 / 16;  // 16-byte chunks per row
-  for (int i = threadIdx.x; i < kRows * kChunks; i += blockDim.x) {
-    const int r = i / kChunks;
-    const int cch = i - r * kChunks;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < valid) v = __ldg(reinterpret_cast<const uint4*>(src + (int64_t)r * row_stride) + cch);
-    *reinterpret_cast<uint4*>(tile + r * pitch + cch * 16) = v;
-  }
-}
-
-// Rotated (or plain, for D = 96) fp32 values of `N` consecutive channels of a smem row starting at c0.
+// fp32 values of N consecutive channels of one token row read straight from global memory (16-byte
+// loads; the row's bytes are contiguous), rotated by the Walsh-Hadamard transform when `rot`.
+// Rows past the end of the sequence read as zeros.
 template <int N, typename T>
-__device__ __forceinline__ void row_values(const uint8_t* row, int c0, bool rot, float* x) {
-  const T* r = reinterpret_cast<const T*>(row) + c0;
+__device__ __forceinline__ void row_values(const T* __restrict__ row, bool valid, bool rot, float* x) {
+  uint4 v[N / 8];
 #pragma unroll
-  for (int i = 0; i < N; i += 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(r + i);
-    const T* e = reinterpret_cast<const T*>(&v);
+  for (int i = 0; i < N / 8; ++i)
+    v[i] = valid ? __ldg(reinterpret_cast<const uint4*>(row) + i) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) x[i + k] = to_f32<T>(e[k]);
+  for (int i = 0; i < N / 8; ++i) {
+    const T* e = reinterpret_cast<const T*>(&v[i]);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) x[i * 8 + k] = to_f32<T>(e[k]);
   }
   if (rot) fwht<N>(x);
 }
@@ -93,17 +92,19 @@ __device__ __forceinline__ float abs_max(const float* x) {
   return m;
 }
 
+// int8 codes of x[0..N) with `scale`, written as 16-byte stores to dst (global memory).
 template <int N>
 __device__ __forceinline__ void store_codes(const float* x, float scale, int8_t* dst) {
+  const float rcp = __frcp_rn(scale);
 #pragma unroll
   for (int i = 0; i < N; i += 16) {
     uint32_t w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int c0 = quant_code(x[i + 4 * k + 0], scale);
-      const int c1 = quant_code(x[i + 4 * k + 1], scale);
-      const int c2 = quant_code(x[i + 4 * k + 2], scale);
-      const int c3 = quant_code(x[i + 4 * k + 3], scale);
+      const int c0 = quant_code(x[i + 4 * k + 0], scale, rcp);
+      const int c1 = quant_code(x[i + 4 * k + 1], scale, rcp);
+      const int c2 = quant_code(x[i + 4 * k + 2], scale, rcp);
+      const int c3 = quant_code(x[i + 4 * k + 3], scale, rcp);
       w[k] = (uint32_t)(c0 & 0xff) | ((uint32_t)(c1 & 0xff) << 8) | ((uint32_t)(c2 & 0xff) << 16) |
              ((uint32_t)(c3 & 0xff) << 24);
     }
@@ -111,75 +112,60 @@ __device__ __forceinline__ void store_codes(const float* x, float scale, int8_t*
   }
 }
 
-// Quantise one smem row (thread-private) to DK int8 codes with scale = max(rowmax, floor)/127, where
-// the scale's amax comes from `amax_fn` (the row's own amax for Q, the 32-row block amax for K).
-// D = 256 is two independent 128-wide rotation blocks sharing one scale; the first block is
-// recomputed after the scale is known so that only 128 values are live at a time.
+// Quantise one token row to DK int8 codes (written to out_row when `store`) with
+// scale = max(amax_fn(row amax), 1e-12) / 127: the row's own amax for Q, the 32-row block amax for K
+// (amax_fn is a warp reduction, so every lane of the warp calls it).  D = 256 is two independent
+// 128-wide rotation blocks sharing one scale; the first block is reloaded and recomputed after the
+// scale is known so that only 128 values are live at a time.
 template <int D, typename T, typename AmaxFn>
-__device__ __forceinline__ float quant_row(const uint8_t* row, int8_t* out_row, AmaxFn amax_fn) {
+__device__ __forceinline__ float quant_row(const T* __restrict__ row, bool valid, int8_t* out_row, bool store,
+                                           AmaxFn amax_fn) {
   constexpr bool kRot = (D & (D - 1)) == 0;
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
   if constexpr (D == 256) {
     float x[128];
-    row_values<128, T>(row, 0, true, x);
+    row_values<128, T>(row, valid, true, x);
     const float a0 = abs_max<128>(x);
-    row_values<128, T>(row, 128, true, x);
+    row_values<128, T>(row + 128, valid, true, x);
     const float a1 = abs_max<128>(x);
     const float scale = __fdiv_rn(fmaxf(amax_fn(fmaxf(a0, a1)), 1e-12f), 127.0f);
-    store_codes<128>(x, scale, out_row + 128);
-    row_values<128, T>(row, 0, true, x);
-    store_codes<128>(x, scale, out_row);
+    if (store) store_codes<128>(x, scale, out_row + 128);
+    row_values<128, T>(row, valid, true, x);
+    if (store) store_codes<128>(x, scale, out_row);
     return scale;
   } else {
     float x[DK];
-    row_values<D, T>(row, 0, kRot, x);
+    row_values<D, T>(row, valid, kRot, x);
 #pragma unroll
     for (int i = D; i < DK; ++i) x[i] = 0.f;
     const float scale = __fdiv_rn(fmaxf(amax_fn(abs_max<D>(x)), 1e-12f), 127.0f);
-    store_codes<DK>(x, scale, out_row);
+    if (store) store_codes<DK>(x, scale, out_row);
     return scale;
   }
 }
 
-template <int D>
-constexpr int tile_pitch() {
-  return D * 2 + 16;  // bytes; the 16-byte skew keeps per-thread row reads free of bank conflicts
-}
-
 // ------------------------------------------------------------------------------------------------
-// Q
+// Q: one thread per token row
 // ------------------------------------------------------------------------------------------------
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
                                                         float fold, int8_t* __restrict__ q8, float* __restrict__ qs) {
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
-  constexpr int PITCH = tile_pitch<D>();
-  extern __shared__ __align__(16) uint8_t qsm[];
-  uint8_t* tile = qsm;
-  int8_t* codes = reinterpret_cast<int8_t*>(qsm + kRows * PITCH);
-  const int s0 = blockIdx.x * kRows;
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int h = bh - b * H;
-  const int valid = min(kRows, S - s0);
-  load_tile<D, T>(x + (int64_t)b * st.b + (int64_t)s0 * st.s + (int64_t)h * st.h, st.s, valid, tile, PITCH);
-  __syncthreads();
-  const int r = threadIdx.x;
-  float scale = quant_row<D, T>(tile + r * PITCH, codes + r * DK, [](float a) { return a; });
-  if (r < valid) {
-    float s = scale;
-    if ((D & (D - 1)) == 0) s = s / (float)(D < 128 ? D : 128);
-    qs[(int64_t)bh * S + s0 + r] = s * fold;
+  const int s = blockIdx.x * kRows + threadIdx.x;
+  const bool valid = s < S;
+  const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h;
+  float scale = quant_row<D, T>(row, valid, q8 + ((int64_t)bh * S + s) * DK, valid, [](float a) { return a; });
+  if (valid) {
+    if ((D & (D - 1)) == 0) scale = scale / (float)(D < 128 ? D : 128);
+    qs[(int64_t)bh * S + s] = scale * fold;
   }
-  __syncthreads();
-  // rows of one (b, h) are contiguous in q8: the CTA's output is one block of valid*DK bytes
-  int8_t* dst = q8 + ((int64_t)bh * S + s0) * DK;
-  for (int i = threadIdx.x; i < valid * DK / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(codes)[i];
 }
 
 // ------------------------------------------------------------------------------------------------
-// K + V
+// K + V: one thread per key row; a warp is one 32-key K scale block
 // ------------------------------------------------------------------------------------------------
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
@@ -187,66 +173,42 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
                                                          int8_t* __restrict__ k8, float* __restrict__ ks,
                                                          uint8_t* __restrict__ v8t) {
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
-  constexpr int PITCH = tile_pitch<D>();
-  extern __shared__ __align__(16) uint8_t kvsm[];
-  uint8_t* tile = kvsm;                                             // K tile, then V tile
-  int8_t* codes = reinterpret_cast<int8_t*>(kvsm + kRows * PITCH);  // [kRows][DK]
-  uint8_t* vt = kvsm + kRows * PITCH + kRows * DK;                  // [D][kRows] e4m3
-  float* fac = reinterpret_cast<float*>(vt + D * kRows);            // [D]
   const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
-  const int s0 = blockIdx.x * kRows;
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int h = bh - b * H;
-  const int valid = max(0, min(kRows, S - s0));
-  const int rows_out = min(kRows, spad - s0);  // rows of this tile inside the padded tensors
-  const int r = threadIdx.x;
-  const int lane = r & 31;
-
-  for (int c = threadIdx.x; c < D; c += blockDim.x)
-    fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
-
-  // K: one scale per 32-key block = one warp
-  load_tile<D, T>(k + (int64_t)b * sk.b + (int64_t)s0 * sk.s + (int64_t)h * sk.h, sk.s, valid, tile, PITCH);
+  const int s = blockIdx.x * kRows + threadIdx.x;
+  __shared__ float fac[D];   // per-channel V factor 448 / max(amax, 1e-30) (sage_quant.py:68-69)
+  for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
   __syncthreads();
-  const float kscale = quant_row<D, T>(tile + r * PITCH, codes + r * DK, [](float a) {
+  if (s - (int)(threadIdx.x & 31) >= spad) return;   // whole warp past the padded length
+  const bool valid = s < S;        // real key (rows in [S, spad) are zero padding)
+  const bool inpad = s < spad;     // row exists in the padded tensors
+  const int lane = threadIdx.x & 31;
+
+  // K: codes and the block scale (warp max of the 32 rows' amax)
+  const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h;
+  const float kscale = quant_row<D, T>(krow, valid, k8 + ((int64_t)bh * spad + s) * DK, inpad, [](float a) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
   });
-  if (lane == 0 && r < rows_out) ks[(int64_t)bh * (spad / kKvBlock) + (s0 + r) / kKvBlock] = kscale;
-  __syncthreads();
-  {
-    int8_t* dst = k8 + ((int64_t)bh * spad + s0) * DK;
-    for (int i = threadIdx.x; i < rows_out * DK / 16; i += blockDim.x)
-      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(codes)[i];
-  }
+  if (lane == 0) ks[(int64_t)bh * (spad / kKvBlock) + s / kKvBlock] = kscale;
 
-  // V: per-channel scale to e4m3, transposed into [D][keys]
-  load_tile<D, T>(v + (int64_t)b * sv.b + (int64_t)s0 * sv.s + (int64_t)h * sv.h, sv.s, valid, tile, PITCH);
-  __syncthreads();
-  {
-    const T* row = reinterpret_cast<const T*>(tile + r * PITCH);
-#pragma unroll 4
-    for (int c = 0; c < D; c += 8) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(row + c);
-      const T* e = reinterpret_cast<const T*>(&raw);
+  // V: per-channel scale to e4m3; channel c of this key goes to v8t[b, h, c, s] (32 lanes = 32
+  // consecutive bytes of each channel row)
+  if (!inpad) return;
+  const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h;
+  uint8_t* vout = v8t + (int64_t)bh * D * spad + s;
+#pragma unroll 2
+  for (int c = 0; c < D; c += 8) {
+    const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(vrow + c)) : make_uint4(0, 0, 0, 0);
+    const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int kx = 0; kx < 8; kx += 2) {
-        float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
-        float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
-        const uint16_t pk = pack_e4m3x2(y0, y1);
-        vt[(c + kx) * kRows + r] = (uint8_t)(pk & 0xff);
-        vt[(c + kx + 1) * kRows + r] = (uint8_t)(pk >> 8);
-      }
-    }
-  }
-  __syncthreads();
-  {
-    const int chunks = rows_out / 16;  // 16-byte chunks per channel row
-    for (int i = threadIdx.x; i < D * chunks; i += blockDim.x) {
-      const int c = i / chunks;
-      const int q = i - c * chunks;
-      *reinterpret_cast<uint4*>(v8t + ((int64_t)bh * D + c) * spad + s0 + q * 16) =
-          *reinterpret_cast<const uint4*>(vt + c * kRows + q * 16);
+    for (int kx = 0; kx < 8; kx += 2) {
+      const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
+      const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
+      const uint16_t pk = pack_e4m3x2(y0, y1);
+      vout[(int64_t)(c + kx) * spad] = (uint8_t)(pk & 0xff);
+      vout[(int64_t)(c + kx + 1) * spad] = (uint8_t)(pk >> 8);
     }
   }
 }
@@ -296,15 +258,6 @@ __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, in
 // ------------------------------------------------------------------------------------------------
 // host launchers
 // ------------------------------------------------------------------------------------------------
-template <int D>
-constexpr int q_smem() {
-  return kRows * tile_pitch<D>() + kRows * (D == 64 ? 64 : (D == 256 ? 256 : 128));
-}
-template <int D>
-constexpr int kv_smem() {
-  return q_smem<D>() + D * kRows + D * 4;
-}
-
 static int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -317,24 +270,18 @@ static int check_launch(const char* what) {
 template <int D, typename T>
 static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold, int8_t* q8, float* qs,
                      cudaStream_t stream) {
-  auto kern = quant_q_kernel<D, T>;
-  constexpr int smem = q_smem<D>();
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((S + kRows - 1) / kRows, B * H);
-  kern<<<grid, kRows, smem, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs);
+  quant_q_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs);
   return check_launch("quant_q");
 }
 
 template <int D, typename T>
 static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
                       int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream) {
-  auto kern = quant_kv_kernel<D, T>;
-  constexpr int smem = kv_smem<D>();
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   const int spad = (int)kv_pad(S);
   dim3 grid((spad + kRows - 1) / kRows, B * H);
-  kern<<<grid, kRows, smem, stream>>>(reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), S, H, sk, sv, vs,
-                                      k8, ks, v8t);
+  quant_kv_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), S,
+                                                    H, sk, sv, vs, k8, ks, v8t);
   return check_launch("quant_kv");
 }
 

@@ -67,6 +67,17 @@ class KernelBackend:
                                         _attention.status_word(out.device).data_ptr(), self.stream), "sage_attn_fwd")
 
 
+def _gather(x: torch.Tensor, world: int, group) -> torch.Tensor:
+    """[world, *x.shape]: every rank's x, in rank order (NCCL writes straight into one buffer)."""
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((world,) + tuple(x.shape), device=x.device, dtype=x.dtype)
+        dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+        return out
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x.contiguous(), group=group)
+    return torch.stack(parts)
+
+
 def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=None):
     """Context-parallel attention over `group`.
 
@@ -86,13 +97,15 @@ def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=Non
     dk = be.qk_row_bytes(D)
     # 1. global V channel amax
     vs = torch.zeros((B, Hkv, D), device=dev, dtype=torch.float32)
-    be.v_amax(v, vs)
+    if Sr > 0:
+        be.v_amax(v, vs)
     dist.all_reduce(vs, op=dist.ReduceOp.MAX, group=group)
     # 2. local quantisation; every rank's K chunk is quantised to `per` rows (zero rows past its end)
     fold = float(_attention.sm_fold(sm_scale, D))
     q8 = torch.empty((B, H, Sr, dk), device=dev, dtype=torch.int8)
     qs = torch.empty((B, H, Sr), device=dev, dtype=torch.float32)
-    be.quant_q(q, fold, q8, qs)
+    if Sr > 0:
+        be.quant_q(q, fold, q8, qs)
     k8 = torch.zeros((B, Hkv, per, dk), device=dev, dtype=torch.int8)
     ks = torch.zeros((B, Hkv, per // KV_BLOCK), device=dev, dtype=torch.float32)
     v8t = torch.zeros((B, Hkv, D, per), device=dev, dtype=torch.uint8)
@@ -106,12 +119,9 @@ def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=Non
         ks[:, :, :spad // KV_BLOCK] = ks_l
         v8t[..., :spad] = v8t_l
     # 3. all-gather the quantised keys and values, then reassemble [B, Hkv, world*per, ...]
-    g_k8 = torch.empty((world,) + tuple(k8.shape), device=dev, dtype=torch.int8)
-    g_ks = torch.empty((world,) + tuple(ks.shape), device=dev, dtype=torch.float32)
-    g_v8 = torch.empty((world,) + tuple(v8t.shape), device=dev, dtype=torch.uint8)
-    dist.all_gather_into_tensor(g_k8, k8, group=group)
-    dist.all_gather_into_tensor(g_ks, ks, group=group)
-    dist.all_gather_into_tensor(g_v8, v8t, group=group)
+    g_k8 = _gather(k8, world, group)
+    g_ks = _gather(ks, world, group)
+    g_v8 = _gather(v8t, world, group)
     spad_total = world * per
     k8_full = g_k8.permute(1, 2, 0, 3, 4).reshape(B, Hkv, spad_total, dk)
     ks_full = g_ks.permute(1, 2, 0, 3).reshape(B, Hkv, spad_total // KV_BLOCK)

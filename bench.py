@@ -8,8 +8,9 @@ larger than the 126 MB L2, so consecutive steps do not hit in L2.
 
 Prints one JSON line (rank 0):
   value      effective TOPS (4*B*H*N^2*D / time) of the whole job, inputs resident in HBM, CUDA events
-  e2e        same metric through the public API with pinned host inputs copied in and the output copied
-             out inside every step
+  e2e        same metric through the public host-memory API (rdna4_sage.attention_host) with pinned host
+             inputs copied in and the output copied out inside every step (copies overlapped with the
+             kernels chunk by chunk); the unpipelined copy + sageattn + copy sequence is reported beside it
   roofline   the attention kernel timed alone (CUDA events around sage_attn_fwd) against the dense
              8-bit tensor peak = 2 x the measured bf16 cuBLAS peak in MEASURED_PEAKS.json
   cpu_baseline  the reference's CPU path for this call (torch SDPA in bf16 on the host cores, the route
@@ -182,7 +183,12 @@ def run_reference(args):
 
 
 def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
-    """Time the public API with pinned host inputs copied in and the output copied out every step."""
+    """Time the public API with pinned host inputs copied in and the output copied out every step.
+
+    Headline: rdna4_sage.attention_host (one C-ABI call; chunks of heads copied in, attended and copied
+    out on three streams, so the copies overlap the kernels).  Also timed: the unpipelined sequence a
+    caller of the device API writes (copy Q, K, V in; sageattention.sageattn; copy the output out)."""
+    import rdna4_sage
     import sageattention
 
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -190,21 +196,30 @@ def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
 
-    def e2e_step():
+    def host_step():
+        rdna4_sage.attention_host(hq, hk, hv, "NHD", out=hout, non_blocking=True)
+
+    def device_api_step():
         dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
         o = sageattention.sageattn(dq, dk, dv, tensor_layout="NHD")
         hout.copy_(o, non_blocking=True)
 
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    n = max(2, args.steps // 2)
-    e0.record(stream)
-    for _ in range(n):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    return max_over_ranks(e0.elapsed_time(e1) / n), h2d, d2h
+    res = {}
+    for name, fn in (("host", host_step), ("device_api", device_api_step)):
+        for _ in range(2):
+            fn()
+        barrier()
+        n = max(2, args.steps // 2)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        res[name] = max_over_ranks(e0.elapsed_time(e1) / n)
+    from rdna4_sage import _lib
+    B_, S_, H_, D_ = q.shape
+    hpc = _lib.lib().sage_host_heads_per_chunk(B_, H_, H_, S_, S_, D_, 0)
+    return res["host"], res["device_api"], hpc, h2d, d2h
 
 
 HUNYUAN = (1, 24, 67576, 128)
@@ -327,9 +342,9 @@ def run_ours(args):
     value = total_ops / (ms * 1e-3) / 1e12
 
     # ---- e2e: public API with pinned host buffers, copies inside every step
-    ms_e2e, h2d, d2h = None, 0, 0
+    ms_e2e, ms_e2e_dev, hpc, h2d, d2h = None, None, 0, 0, 0
     if not args.no_e2e:
-        ms_e2e, h2d, d2h = run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks)
+        ms_e2e, ms_e2e_dev, hpc, h2d, d2h = run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks)
 
     # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream)
     L = _lib.lib()
@@ -415,7 +430,10 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "e2e": None if ms_e2e is None else
             {"value": total_ops / (ms_e2e * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": ms_e2e,
-             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+             "api": f"rdna4_sage.attention_host (sage_attention_host), {hpc} heads per chunk, copies overlapped",
+             "device_api": {"value": total_ops / (ms_e2e_dev * 1e-3) / 1e12, "ms_per_step": ms_e2e_dev,
+                            "api": "copy in + sageattention.sageattn + copy out, unpipelined"}},
             "gpu_launches": 4 * args.steps,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
                          "frac": achieved / peak_tops, "traffic": traffic,

@@ -102,6 +102,23 @@ int sage_attention_static(const void* q, const void* k, const void* v, int dtype
                           int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out,
                           int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream);
 
+/* sage_attention on tensors in HOST memory (pinned for overlap; strides as above, channel axis contiguous,
+ * no alignment rule for the host pointers): q, k, v, out and lse (nullable, [B, H, Sq]) are host
+ * pointers.  The heads are cut into chunks of `heads_per_chunk` query heads (a multiple of H / Hkv;
+ * 0 = chosen by the library); each chunk is copied in on a library-owned stream, attended on `stream`
+ * and copied out on a second library stream, so copies and kernels of neighbouring chunks overlap.
+ * When the work on `stream` completes, `out` and `lse` hold the result.  `workspace` is device memory
+ * of sage_host_workspace_bytes(...) bytes (256-byte aligned) for two chunks in flight plus the quantised
+ * tensors.  The reference has no such entry (its callers copy to the GPU themselves and call
+ * attention(), _attention.py:97); this one replaces that copy + attention() + copy-back sequence. */
+int sage_host_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk);
+size_t sage_host_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk);
+int sage_attention_host(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
+                        int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh,
+                        int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb,
+                        int64_t oss, int64_t osh, float* lse, int heads_per_chunk, void* workspace,
+                        size_t workspace_bytes, int* status, void* stream);
+
 /* Synchronise `stream`, read and clear a status word (NULL = the library's own word on the current
  * device); returns the code it held (SAGE_OK when no kernel reported an error). */
 int sage_status_sync(int* status, void* stream);

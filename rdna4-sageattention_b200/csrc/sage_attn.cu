@@ -543,6 +543,15 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   return kStatusOk;
 }
 
+int attention_rows_per_cta(int D) {
+  switch (D) {
+    case 64: return AttnCfg<64>::QT * 128;
+    case 96: return AttnCfg<96>::QT * 128;
+    case 128: return AttnCfg<128>::QT * 128;
+    default: return AttnCfg<256>::QT * 128;
+  }
+}
+
 int launch_attention(const AttnArgs& a, cudaStream_t stream) {
   switch (a.D) {
     case 64: return a.causal ? launch_attention_t<64, true>(a, stream) : launch_attention_t<64, false>(a, stream);

@@ -1,0 +1,280 @@
+// sage_attention_host: the whole attention call on tensors in host memory.  The heads are cut into
+// chunks (whole groups of query heads sharing a kv head); chunk c is copied in on one stream, attended
+// on the caller's stream and copied out on a third, so the host<->device copies of neighbouring chunks
+// overlap the kernels of the current one.  Device staging for two chunks in flight is carved from the
+// caller's workspace; the library allocates nothing.
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "../../include/sage_b200.h"
+#include "sage_internal.h"
+
+namespace sage {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Per-device copy streams and the events that order the two staging slots.
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t in = nullptr, out = nullptr;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t in_done[2] = {nullptr, nullptr};
+  cudaEvent_t comp_done[2] = {nullptr, nullptr};
+  cudaEvent_t out_done[2] = {nullptr, nullptr};
+};
+
+std::mutex g_pipe_mu;
+HostPipe g_pipe[kMaxDevices];
+
+// Called with g_pipe_mu held.
+HostPipe* pipe_for_current_device(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  *dev_out = dev;
+  HostPipe& p = g_pipe[dev];
+  if (p.ready) return &p;
+  bool ok = cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking) == cudaSuccess &&
+            cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming) == cudaSuccess;
+  for (int i = 0; ok && i < 2; ++i)
+    ok = cudaEventCreateWithFlags(&p.in_done[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p.comp_done[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&p.out_done[i], cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) return nullptr;
+  p.ready = true;
+  return &p;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Layout of one tensor's chunk on the device: token-major (B, S, hg, D) when the host tensor keeps a
+// token's heads next to each other (head stride == D, e.g. NHD), so each batch is one pitched copy;
+// head-major (B, hg, S, D) otherwise (HND and other layouts).
+struct ChunkLayout {
+  bool token_major;
+  Strides3 st;  // element strides of the device chunk
+};
+
+ChunkLayout chunk_layout(const Strides3& host, int S, int hg, int D) {
+  if (host.h == D) return {true, Strides3{(int64_t)S * hg * D, (int64_t)hg * D, D}};
+  return {false, Strides3{(int64_t)hg * S * D, D, (int64_t)S * D}};
+}
+
+// Copies heads [h0, h0 + hg) of a (B, S, H, D) tensor with host strides `hs` to (to_dev) or from the
+// device chunk `dev` laid out as `L`, with one cudaMemcpyAsync / cudaMemcpy2DAsync per contiguous run.
+cudaError_t copy_heads(char* dev, char* host, bool to_dev, int B, int S, int h0, int hg, int D, size_t es,
+                       const Strides3& hs, const ChunkLayout& L, cudaStream_t st) {
+  const cudaMemcpyKind kind = cudaMemcpyDefault;
+  const size_t row = (size_t)D * es;
+  for (int b = 0; b < B; ++b) {
+    char* hb = host + ((int64_t)b * hs.b + (int64_t)h0 * hs.h) * (int64_t)es;
+    char* db = dev + (int64_t)b * L.st.b * (int64_t)es;
+    cudaError_t e = cudaSuccess;
+    if (L.token_major) {
+      const size_t width = (size_t)hg * row, hp = (size_t)hs.s * es;
+      e = to_dev ? cudaMemcpy2DAsync(db, width, hb, hp, width, S, kind, st)
+                 : cudaMemcpy2DAsync(hb, hp, db, width, width, S, kind, st);
+    } else if (hs.s == D && hs.h == (int64_t)S * D) {
+      const size_t n = (size_t)hg * S * row;  // the chunk's heads are one contiguous run
+      e = to_dev ? cudaMemcpyAsync(db, hb, n, kind, st) : cudaMemcpyAsync(hb, db, n, kind, st);
+    } else {
+      for (int h = 0; h < hg && e == cudaSuccess; ++h) {
+        char* hh = hb + (int64_t)h * hs.h * (int64_t)es;
+        char* dh = db + (int64_t)h * L.st.h * (int64_t)es;
+        if (hs.s == D) {
+          e = to_dev ? cudaMemcpyAsync(dh, hh, (size_t)S * row, kind, st)
+                     : cudaMemcpyAsync(hh, dh, (size_t)S * row, kind, st);
+        } else {
+          const size_t hp = (size_t)hs.s * es;
+          e = to_dev ? cudaMemcpy2DAsync(dh, row, hh, hp, row, S, kind, st)
+                     : cudaMemcpy2DAsync(hh, hp, dh, row, row, S, kind, st);
+        }
+      }
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Staging bytes of one slot: the chunk's Q, K, V and output in the input dtype plus its LSE rows.
+size_t slot_bytes(int B, int hg, int hkg, int Sq, int Skv, int D, size_t es) {
+  return 2 * align256((size_t)B * Sq * hg * D * es) + 2 * align256((size_t)B * Skv * hkg * D * es) +
+         align256((size_t)B * hg * Sq * 4);
+}
+
+// Chunk size in query heads when the caller passes 0: a small simulation of the three-stage pipeline
+// (copy in, compute with whole waves of CTAs, copy out) over every multiple of the group size, with
+// nominal rates for a PCIe 5.0 x16 link and the attention kernel.  The rates only rank the candidates.
+int auto_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D) {
+  const int G = H / Hkv;
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (nsm <= 0) nsm = 148;
+  const double link = 50e9;      // bytes/s each way
+  const double rate = 1.2e15;    // attention operations/s
+  const double launch = 20e-6;   // per-chunk launch and tail overhead, s
+  const double es = 2.0;
+  const double tiles_per_head = (double)B * ((Sq + attention_rows_per_cta(D) - 1) / attention_rows_per_cta(D));
+  const double t_in_q = (double)B * Sq * D * es / link, t_in_kv = 2.0 * B * Skv * D * es / link;
+  const double t_out = (double)B * Sq * D * es / link;
+  const double t_head = 4.0 * B * Sq * (double)Skv * D / rate;   // one head's kernel time
+  const double t_wave = t_head * nsm / tiles_per_head;           // one full wave of CTAs
+  int best = H;
+  double best_t = 1e30;
+  for (int hkg = 1; hkg <= Hkv; ++hkg) {
+    const int hg = hkg * G;
+    const int nch = (H + hg - 1) / hg;
+    double in_end = 0, comp_end = 0, out_end = 0, comp_prev[2] = {0, 0}, out_prev[2] = {0, 0};
+    for (int c = 0; c < nch; ++c) {
+      const int hc = std::min(hg, H - c * hg);
+      const double tin = hc * t_in_q + (hc / G) * t_in_kv;
+      const double tc = launch + std::ceil(hc * tiles_per_head / nsm) * t_wave;
+      in_end = std::max(in_end, comp_prev[c & 1]) + tin;
+      comp_end = std::max(std::max(comp_end, in_end), out_prev[c & 1]) + tc;
+      out_end = std::max(out_end, comp_end) + hc * t_out;
+      comp_prev[c & 1] = comp_end;
+      out_prev[c & 1] = out_end;
+    }
+    if (out_end < best_t * 0.999) {
+      best_t = out_end;
+      best = hg;
+    }
+  }
+  return best;
+}
+
+int resolve_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D, int hpc) {
+  if (hpc <= 0) return auto_heads_per_chunk(B, H, Hkv, Sq, Skv, D);
+  const int G = H / Hkv;
+  if (hpc % G != 0) return -1;
+  return std::min(hpc, H);
+}
+
+}  // namespace
+}  // namespace sage
+
+using namespace sage;
+
+extern "C" {
+
+int sage_host_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk) {
+  if (sage_qk_row_bytes(D) == 0 || B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0 || Sq <= 0 || Skv <= 0) return 0;
+  const int hg = resolve_heads_per_chunk(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
+  return hg > 0 ? hg : 0;
+}
+
+size_t sage_host_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk) {
+  const int hg = sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
+  if (hg == 0) return 0;
+  const int hkg = hg / (H / Hkv);
+  return 2 * slot_bytes(B, hg, hkg, Sq, Skv, D, 2) + align256(sage_workspace_bytes(B, hg, hkg, Sq, Skv, D));
+}
+
+int sage_attention_host(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
+                        int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh,
+                        int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb,
+                        int64_t oss, int64_t osh, float* lse, int heads_per_chunk, void* workspace,
+                        size_t workspace_bytes, int* status, void* stream) {
+  if (dtype != SAGE_BF16 && dtype != SAGE_F16) {
+    set_error("dtype %d (SAGE_BF16 or SAGE_F16 required)", dtype);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) {
+    set_error("q, k, v and out must be non-null");
+    return SAGE_ERR_INVALID;
+  }
+  const int hg = sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
+  if (hg == 0) {
+    set_error("unsupported sizes or heads_per_chunk %d (B=%d H=%d Hkv=%d Sq=%d Skv=%d D=%d)", heads_per_chunk, B, H,
+              Hkv, Sq, Skv, D);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  const size_t need = sage_host_workspace_bytes(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
+  if (workspace == nullptr || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u)) {
+    set_error("workspace of %zu bytes (256-byte aligned) required, got %zu", need, workspace_bytes);
+    return SAGE_ERR_INVALID;
+  }
+  const int G = H / Hkv, hkg = hg / G;
+  const size_t es = 2;
+  const Strides3 hq{qsb, qss, qsh}, hk{ksb, kss, ksh}, hv{vsb, vss, vsh}, ho{osb, oss, osh};
+  // carve: slot 0, slot 1, then the quantised-tensor scratch shared by the (serialised) chunk calls
+  char* base = static_cast<char*>(workspace);
+  struct Slot {
+    char *q, *k, *v, *o;
+    float* lse;
+  } slot[2];
+  size_t off = 0;
+  for (int s = 0; s < 2; ++s) {
+    slot[s].q = base + off;
+    off += align256((size_t)B * Sq * hg * D * es);
+    slot[s].k = base + off;
+    off += align256((size_t)B * Skv * hkg * D * es);
+    slot[s].v = base + off;
+    off += align256((size_t)B * Skv * hkg * D * es);
+    slot[s].o = base + off;
+    off += align256((size_t)B * Sq * hg * D * es);
+    slot[s].lse = reinterpret_cast<float*>(base + off);
+    off += align256((size_t)B * hg * Sq * 4);
+  }
+  char* scratch = base + off;
+  const size_t scratch_bytes = need - off;
+
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  int dev = 0;
+  HostPipe* P = pipe_for_current_device(&dev);
+  if (P == nullptr) {
+    set_error("could not create the copy streams on the current device");
+    return SAGE_ERR_LAUNCH;
+  }
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  auto fail = [](cudaError_t e, const char* what) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  };
+  cudaError_t e = cudaEventRecord(P->start, cs);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(P->in, P->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(P->out, P->start, 0);
+  if (e != cudaSuccess) return fail(e, "stream join");
+  const int nch = (H + hg - 1) / hg;
+  for (int c = 0; c < nch; ++c) {
+    const int s = c & 1, h0 = c * hg, hc = std::min(hg, H - h0), kv0 = h0 / G, hkc = hc / G;
+    Slot& S = slot[s];
+    // copy in: the slot is free once chunk c-2's kernels have read it
+    if (c >= 2) e = cudaStreamWaitEvent(P->in, P->comp_done[s], 0);
+    if (e == cudaSuccess)
+      e = copy_heads(S.q, (char*)q, true, B, Sq, h0, hc, D, es, hq, chunk_layout(hq, Sq, hc, D), P->in);
+    if (e == cudaSuccess)
+      e = copy_heads(S.k, (char*)k, true, B, Skv, kv0, hkc, D, es, hk, chunk_layout(hk, Skv, hkc, D), P->in);
+    if (e == cudaSuccess)
+      e = copy_heads(S.v, (char*)v, true, B, Skv, kv0, hkc, D, es, hv, chunk_layout(hv, Skv, hkc, D), P->in);
+    if (e == cudaSuccess) e = cudaEventRecord(P->in_done[s], P->in);
+    if (e != cudaSuccess) return fail(e, "copy in");
+    // compute on the caller's stream, once the inputs are in and chunk c-2's output has left the slot
+    e = cudaStreamWaitEvent(cs, P->in_done[s], 0);
+    if (e == cudaSuccess && c >= 2) e = cudaStreamWaitEvent(cs, P->out_done[s], 0);
+    if (e != cudaSuccess) return fail(e, "stream wait");
+    const ChunkLayout cq = chunk_layout(hq, Sq, hc, D), ck = chunk_layout(hk, Skv, hkc, D),
+                      cv = chunk_layout(hv, Skv, hkc, D), co = chunk_layout(ho, Sq, hc, D);
+    int rc = sage_attention(S.q, S.k, S.v, dtype, B, hc, hkc, Sq, Skv, D, cq.st.b, cq.st.s, cq.st.h, ck.st.b, ck.st.s,
+                            ck.st.h, cv.st.b, cv.st.s, cv.st.h, sm_scale, causal, S.o, co.st.b, co.st.s, co.st.h,
+                            lse != nullptr ? S.lse : nullptr, scratch, scratch_bytes, status, stream);
+    if (rc != SAGE_OK) return rc;
+    e = cudaEventRecord(P->comp_done[s], cs);
+    // copy out
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(P->out, P->comp_done[s], 0);
+    if (e == cudaSuccess) e = copy_heads(S.o, (char*)out, false, B, Sq, h0, hc, D, es, ho, co, P->out);
+    if (e == cudaSuccess && lse != nullptr)
+      e = cudaMemcpy2DAsync(lse + (size_t)h0 * Sq, (size_t)H * Sq * 4, S.lse, (size_t)hc * Sq * 4,
+                            (size_t)hc * Sq * 4, B, cudaMemcpyDefault, P->out);
+    if (e == cudaSuccess) e = cudaEventRecord(P->out_done[s], P->out);
+    if (e != cudaSuccess) return fail(e, "copy out");
+  }
+  // the caller's stream completes after the last output copy (the out stream runs its copies in order)
+  e = cudaStreamWaitEvent(cs, P->out_done[(nch - 1) & 1], 0);
+  if (e != cudaSuccess) return fail(e, "stream join");
+  return SAGE_OK;
+}
+
+}  // extern "C"

@@ -53,6 +53,8 @@ struct AttnArgs {
   int causal;
 };
 int launch_attention(const AttnArgs& a, cudaStream_t stream);
+// Query rows one attention CTA owns for head dim D (the grid is B * H * ceil(Sq / rows)).
+int attention_rows_per_cta(int D);
 
 int* default_status_word();
 

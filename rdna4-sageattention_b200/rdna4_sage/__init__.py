@@ -12,9 +12,9 @@ import torch
 from torch.nn.attention.bias import causal_lower_right
 
 from . import ops
-from ._attention import ARCHS, HEAD_DIMS, Unsupported, check_supported, device_arch
+from ._attention import ARCHS, HEAD_DIMS, Unsupported, attention_host, check_supported, device_arch
 
-__all__ = ["sageattn", "attention", "is_available", "Unsupported", "ARCHS", "HEAD_DIMS"]
+__all__ = ["sageattn", "attention", "attention_host", "is_available", "Unsupported", "ARCHS", "HEAD_DIMS"]
 __version__ = "0.2.1+b200"
 
 # The C binding behind F.scaled_dot_product_attention. Apps replace F.scaled_dot_product_attention with

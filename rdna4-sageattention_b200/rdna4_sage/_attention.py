@@ -56,13 +56,21 @@ def check_supported(q, k, v, layout, is_causal=False):
         raise Unsupported(f"layout {layout!r}")
     if not (q.is_cuda and k.device == q.device and v.device == q.device):
         raise Unsupported("tensors must be on one CUDA GPU")
+    _check_arch(q.device)
+    _check_shapes(q, k, v, layout, is_causal)
+
+
+def _check_arch(device):
+    arch = device_arch(device)
+    if arch not in ARCHS:
+        raise Unsupported(f"GPU {arch} is not sm_100 (kernels built for {', '.join(ARCHS)} only)")
+
+
+def _check_shapes(q, k, v, layout, is_causal):
     if q.dtype not in DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
         raise Unsupported(f"dtype {q.dtype}/{k.dtype}/{v.dtype} (fp16 or bf16 required)")
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise Unsupported("4D tensors required")
-    arch = device_arch(q.device)
-    if arch not in ARCHS:
-        raise Unsupported(f"GPU {arch} is not sm_100 (kernels built for {', '.join(ARCHS)} only)")
     hd = q.shape[-1]
     if hd not in HEAD_DIMS or k.shape[-1] != hd or v.shape[-1] != hd:
         raise Unsupported(f"head_dim {hd} (supported {HEAD_DIMS})")
@@ -125,6 +133,70 @@ def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=
     if _CHECK:
         check_status(dev)
     return (out, lse) if return_lse else out
+
+
+def _bsh_host(t: torch.Tensor, layout: str):
+    """(batch, seq, head) element strides of a host tensor; the channel axis must be contiguous."""
+    if t.stride(-1) != 1:
+        t = t.contiguous()
+    st = (t.stride(0), t.stride(2), t.stride(1)) if layout == "HND" else (t.stride(0), t.stride(1), t.stride(2))
+    return t, st
+
+
+def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=False, device=None,
+                   heads_per_chunk=0, out=None, non_blocking=False):
+    """attention() for q, k, v in host memory, with the copies to and from the GPU overlapped with the
+    kernels (chunks of heads: copy in / attend / copy out on three streams, one C-ABI call).
+
+    q, k, v: CPU tensors (pinned memory for the copies to overlap), shapes as for attention().  Returns
+    the result in q's layout, a view of a pinned CPU (B, Sq, H, D) buffer (or of `out`, a CPU tensor of
+    that shape and dtype), and with return_lse also the (B, H, Sq) fp32 LSE on the CPU.  `device`: the GPU to run on
+    (default: the current one).  With non_blocking=True the call returns once the work is enqueued on
+    torch's current stream of that device; the results are valid after that stream synchronises.
+    """
+    if layout not in ("HND", "NHD"):
+        raise Unsupported(f"layout {layout!r}")
+    if q.is_cuda or k.is_cuda or v.is_cuda:
+        raise Unsupported("attention_host takes host tensors; use attention() for GPU tensors")
+    _check_shapes(q, k, v, layout, is_causal)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    _check_arch(dev)
+    L = _lib.lib()
+    if layout == "HND":
+        B, H, Sq, D = q.shape
+        Hkv, Skv = k.shape[1], k.shape[2]
+    else:
+        B, Sq, H, D = q.shape
+        Skv, Hkv = k.shape[1], k.shape[2]
+    q, sq_ = _bsh_host(q, layout)
+    k, sk_ = _bsh_host(k, layout)
+    v, sv_ = _bsh_host(v, layout)
+    if out is None:
+        out = torch.empty((B, Sq, H, D), dtype=q.dtype, pin_memory=True)
+    elif out.is_cuda or out.shape != (B, Sq, H, D) or out.dtype != q.dtype or out.stride(-1) != 1:
+        raise ValueError("out must be a CPU tensor of shape (B, Sq, H, D) in q's dtype, channel axis contiguous")
+    lse = torch.empty((B, H, Sq), dtype=torch.float32, pin_memory=True) if return_lse else None
+    hpc = L.sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, int(heads_per_chunk))
+    if hpc == 0:
+        raise Unsupported(f"heads_per_chunk {heads_per_chunk} (a multiple of H / Hkv = {H // Hkv} required)")
+    with torch.cuda.device(dev):
+        ws_bytes = L.sage_host_workspace_bytes(B, H, Hkv, Sq, Skv, D, hpc)
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+        stream = torch.cuda.current_stream(dev)
+        rc = L.sage_attention_host(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[q.dtype], B, H, Hkv, Sq, Skv, D,
+                                   *sq_, *sk_, *sv_, float(sm_scale or 0.0), int(bool(is_causal)), out.data_ptr(),
+                                   out.stride(0), out.stride(1), out.stride(2),
+                                   lse.data_ptr() if lse is not None else None, hpc, ws.data_ptr(), ws_bytes,
+                                   status_word(dev).data_ptr(), stream.cuda_stream)
+        _lib.check(rc, "sage_attention_host")
+        # the workspace goes back to torch's pool only after the stream has finished with it
+        ws.record_stream(stream)
+        if not non_blocking:
+            stream.synchronize()
+        if _CHECK:
+            check_status(dev)
+    res = out.transpose(1, 2) if layout == "HND" else out
+    return (res, lse) if return_lse else res
 
 
 def sm_fold(sm_scale, head_dim):

@@ -30,22 +30,29 @@ __device__ __forceinline__ float to_f32<__half>(__half v) {
   return __half2float(v);
 }
 
+// One butterfly stage of the Walsh-Hadamard transform (pairs LEN apart), then the next stage.  The
+// stages are template-recursive so every index is a compile-time constant and x stays in registers.
+template <int N, int LEN>
+__device__ __forceinline__ void fwht_stage(float* x) {
+  if constexpr (LEN < N) {
+#pragma unroll
+    for (int i = 0; i < N; i += 2 * LEN) {
+#pragma unroll
+      for (int j = i; j < i + LEN; ++j) {
+        const float a = x[j];
+        const float b = x[j + LEN];
+        x[j] = a + b;
+        x[j + LEN] = a - b;
+      }
+    }
+    fwht_stage<N, 2 * LEN>(x);
+  }
+}
+
 // In-place fast Walsh-Hadamard transform of x[0..N) (natural / Sylvester order, unnormalised).
 template <int N>
 __device__ __forceinline__ void fwht(float* x) {
-#pragma unroll
-  for (int len = 1; len < N; len <<= 1) {
-#pragma unroll
-    for (int i = 0; i < N; i += 2 * len) {
-#pragma unroll
-      for (int j = i; j < i + len; ++j) {
-        const float a = x[j];
-        const float b = x[j + len];
-        x[j] = a + b;
-        x[j + len] = a - b;
-      }
-    }
-  }
+  fwht_stage<N, 1>(x);
 }
 
 // trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32 (the reference's

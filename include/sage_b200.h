@@ -102,6 +102,24 @@ int sage_attention_static(const void* q, const void* k, const void* v, int dtype
                           int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out,
                           int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream);
 
+/* Packed variable-length attention in one call (no host synchronisation): replaces the per-sequence
+ * loop of sageattention.sageattn_varlen (src/sageattention/core.py:66-89), which reads cu_seqlens back
+ * to the host and runs the whole attention() pipeline once per sequence.
+ * q [total_q, H, D], k / v [total_k, Hkv, D], out [total_q, H, D]: element strides of the token and head
+ * axes (channel axis contiguous, 16-byte aligned as above).  cu_seqlens_q / cu_seqlens_k: DEVICE int32
+ * arrays of nseq + 1 offsets (sequence i owns tokens [cu[i], cu[i+1])).  max_seqlen_q / max_seqlen_k
+ * must bound every sequence length.  Each sequence is quantised as its own call would be (its own V
+ * channel amax, K scale blocks starting at its first key), so its rows equal the dense call's.
+ * lse (nullable): [H, total_q] fp32.  Sequences with no keys give zero rows.  The offset tables are
+ * checked on the device: inconsistent tables store SAGE_ERR_INVALID into the status word and the call
+ * then writes nothing.  Causal masks are bottom-right aligned per sequence. */
+size_t sage_varlen_workspace_bytes(int nseq, int H, int Hkv, int total_q, int total_k, int D);
+int sage_attention_varlen(const void* q, const void* k, const void* v, int dtype, int nseq, int H, int Hkv, int D,
+                          const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int max_seqlen_q,
+                          int max_seqlen_k, int total_q, int total_k, int64_t qss, int64_t qsh, int64_t kss,
+                          int64_t ksh, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t oss,
+                          int64_t osh, float* lse, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* sage_attention on tensors in HOST memory (pinned for overlap; strides as above, channel axis contiguous,
  * no alignment rule for the host pointers): q, k, v, out and lse (nullable, [B, H, Sq]) are host
  * pointers.  The heads are cut into chunks of `heads_per_chunk` query heads (a multiple of H / Hkv;

@@ -46,6 +46,13 @@ struct AttnParams {
   int q_groups;  // number of QT*128-row query groups per (batch, head)
   float sm_log2e;
   int out_f16;
+  // packed variable-length batches (cu_q == nullptr: dense): B counts sequences, Sq / Skv are unused
+  const int* cu_q;
+  const int* cu_k;
+  const int* cu_pad;
+  const int* seg_ok;
+  int total_q;
+  int64_t pad_total;
 };
 
 template <int D>
@@ -185,10 +192,34 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int hkv = h / (p.H / p.Hkv);
+  // This CTA's sequence.  Dense: batch b of [B, H, Sq] / [B, Hkv, Skv] tensors.  Varlen: packed sequence
+  // b, whose query rows start at cu_q[b] of the [H, total_q] q8 / qs and whose keys start at the
+  // 32-aligned row cu_pad[b] of the [Hkv, pad_total] k8 / v8t.
+  int Sq = p.Sq, Skv = p.Skv, nkb = p.nkb;
+  int qbase = 0, kbase = 0, zq = b * p.H + h, zk = b * p.Hkv + hkv;
+  int64_t q_off = ((int64_t)b * p.H + h) * p.Sq;               // qs / lse index of query row 0
+  int64_t ks_off = ((int64_t)b * p.Hkv + hkv) * p.nkb;         // ks index of key block 0
+  int64_t out_off = (int64_t)b * p.o_sb + (int64_t)h * p.o_sh;  // out element offset of query row 0
+  if (p.cu_q != nullptr) {
+    if (*p.seg_ok == 0) return;  // the offset tables failed their check (reported in the status word)
+    const int qb = p.cu_q[b], kb0 = p.cu_k[b];
+    Sq = p.cu_q[b + 1] - qb;
+    Skv = p.cu_k[b + 1] - kb0;
+    nkb = (Skv + kKvBlock - 1) / kKvBlock;
+    qbase = qb;
+    kbase = p.cu_pad[b];
+    zq = h;
+    zk = hkv;
+    q_off = (int64_t)h * p.total_q + qb;
+    ks_off = (int64_t)hkv * (p.pad_total / kKvBlock) + kbase / kKvBlock;
+    out_off = (int64_t)qb * p.o_ss + (int64_t)h * p.o_sh;
+    if (grp == 0 && Sq > p.q_groups * QT * 128) atomicCAS(p.status, 0, kStatusInvalid);  // max_seqlen_q too small
+  }
   const int q0 = grp * QT * 128;
-  const int off = p.Skv - p.Sq;
-  int kv_end = p.Skv;
-  if (CAUSAL) kv_end = min(p.Skv, q0 + QT * 128 + off);
+  if (q0 >= Sq) return;  // varlen: this group lies past a shorter sequence (the whole CTA leaves)
+  const int off = Skv - Sq;
+  int kv_end = Skv;
+  if (CAUSAL) kv_end = min(Skv, q0 + QT * 128 + off);
   const int n_tiles = kv_end > 0 ? (kv_end + C::BN - 1) / C::BN : 0;
 
   if (threadIdx.x == 0) {
@@ -225,14 +256,13 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      const int zq = b * p.H + h;
-      const int zk = b * p.Hkv + hkv;
       // Q tiles wholly past the last query row are not loaded (their rows are never stored)
-      const int q_tiles_in = min(QT, (p.Sq - q0 + 127) / 128);
+      const int q_tiles_in = min(QT, (Sq - q0 + 127) / 128);
       mbar_arrive_expect_tx(q_full, q_tiles_in * C::Q_TILE);
       for (int t = 0; t < q_tiles_in; ++t)
         for (int a = 0; a < C::DK / C::SW; ++a)
-          tma_load_3d(sQ + t * C::Q_TILE + a * C::BM * C::SW, &tm_q, q_full, a * C::SW, q0 + t * 128, zq);
+          tma_load_3d(sQ + t * C::Q_TILE + a * C::BM * C::SW, &tm_q, q_full, a * C::SW, qbase + q0 + t * 128,
+                      zq);
       int issued = 0;
       bool ok = true;
       for (int j = 0; j < n_tiles; ++j) {
@@ -244,9 +274,10 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         }
         mbar_arrive_expect_tx(&k_full[st], C::K_TILE);
         for (int a = 0; a < C::DK / C::SW; ++a)
-          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, j * C::BN, zk);
+          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, kbase + j * C::BN,
+                      zk);
         mbar_arrive_expect_tx(&v_full[st], C::V_TILE);
-        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], j * C::BN, 0, zk);
+        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], kbase + j * C::BN, 0, zk);
         issued = j + 1;
       }
       if (!ok) {
@@ -335,16 +366,16 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     const int row = wq * 32 + lane;
     const int q_row = q0 + t * 128 + row;
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
-    const float qsr = __ldg(p.qs + ((int64_t)b * p.H + h) * p.Sq + min(q_row, p.Sq - 1));
+    const float qsr = __ldg(p.qs + q_off + min(q_row, Sq - 1));
     const float c = p.sm_log2e * qsr;
-    const float* ksb = p.ks + ((int64_t)b * p.Hkv + hkv) * p.nkb;
+    const float* ksb = p.ks + ks_off;
     const int last_key = CAUSAL ? q_row + off : 0x7fffffff;
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
     float ksn[4];  // K scales of the next tile, loaded one iteration ahead
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ksn[i] = i < p.nkb ? __ldg(ksb + i) : 0.f;
+    for (int i = 0; i < 4; ++i) ksn[i] = i < nkb ? __ldg(ksb + i) : 0.f;
     for (int j = 0; j < n_tiles; ++j) {
       const int slot = QT == 2 ? t : (j & 1);
       const uint32_t sph = QT == 2 ? (j & 1) : ((j >> 1) & 1);
@@ -354,7 +385,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       for (int i = 0; i < 4; ++i) {
         ksv[i] = ksn[i];
         const int kb = (j + 1) * 4 + i;
-        ksn[i] = kb < p.nkb ? __ldg(ksb + kb) : 0.f;
+        ksn[i] = kb < nkb ? __ldg(ksb + kb) : 0.f;
       }
       if (!mbar_wait(&s_full[slot], sph, wc)) {
         ok = false;
@@ -365,8 +396,8 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 4; ++i) tmem_ld32(tl + slot * 128 + i * 32, s[i]);
       tmem_wait_ld();
-      const bool need_mask = (kv0 + C::BN > p.Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
-      const int lim = min(p.Skv, CAUSAL ? last_key + 1 : p.Skv);  // keys < lim are kept
+      const bool need_mask = (kv0 + C::BN > Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
+      const int lim = min(Skv, CAUSAL ? last_key + 1 : Skv);  // keys < lim are kept
       uint32_t pw[32];
       float sum;
       float m_new;
@@ -405,11 +436,11 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     if (ok && n_tiles > 0) ok = mbar_wait(&o_done[t], (n_tiles - 1) & 1, wc);
     if (ok) {
       tc_fence_after();
-      const float inv = __fdiv_rn(1.0f / 448.0f, l);
+      // a row with no keys (an empty varlen key sequence) gets zeros
+      const float inv = l > 0.f ? __fdiv_rn(1.0f / 448.0f, l) : 0.f;
       const float* vsp = p.vs + ((int64_t)b * p.Hkv + hkv) * D;
-      const bool store = q_row < p.Sq;
-      char* orow = reinterpret_cast<char*>(p.out) +
-                   2 * ((int64_t)b * p.o_sb + (int64_t)(store ? q_row : 0) * p.o_ss + (int64_t)h * p.o_sh);
+      const bool store = q_row < Sq;
+      char* orow = reinterpret_cast<char*>(p.out) + 2 * (out_off + (int64_t)(store ? q_row : 0) * p.o_ss);
 #pragma unroll 1
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
@@ -443,7 +474,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         }
       }
       if (p.lse != nullptr && store)
-        p.lse[((int64_t)b * p.H + h) * p.Sq + q_row] = (m * c + log2f(l)) * 0.69314718055994531f;
+        p.lse[q_off + q_row] = (m * c + log2f(l)) * 0.69314718055994531f;
     }
     tmem_wait_st();
   }
@@ -499,14 +530,17 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
 template <int D, bool CAUSAL>
 static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   using C = AttnCfg<D>;
-  const int64_t skv_pad = kv_pad(a.Skv);
+  const bool varlen = a.cu_q != nullptr;
+  // rows per (batch, head) plane of q8 and of k8 / v8t, and the number of planes
+  const int64_t q_rows = varlen ? a.total_q : a.Sq;
+  const int64_t k_rows = varlen ? a.pad_total : kv_pad(a.Skv);
+  const uint64_t q_planes = varlen ? (uint64_t)a.H : (uint64_t)a.B * a.H;
+  const uint64_t k_planes = varlen ? (uint64_t)a.Hkv : (uint64_t)a.B * a.Hkv;
   CUtensorMap mq, mk, mv;
   const CUtensorMapSwizzle qk_sw = C::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (!make_map(&mq, a.q8, C::DK, a.Sq, (uint64_t)a.B * a.H, C::DK, (uint64_t)a.Sq * C::DK, C::SW, 128, qk_sw) ||
-      !make_map(&mk, a.k8, C::DK, skv_pad, (uint64_t)a.B * a.Hkv, C::DK, (uint64_t)skv_pad * C::DK, C::SW, 128,
-                qk_sw) ||
-      !make_map(&mv, a.v8t, skv_pad, D, (uint64_t)a.B * a.Hkv, skv_pad, (uint64_t)skv_pad * D, 128, D,
-                CU_TENSOR_MAP_SWIZZLE_128B))
+  if (!make_map(&mq, a.q8, C::DK, q_rows, q_planes, C::DK, (uint64_t)q_rows * C::DK, C::SW, 128, qk_sw) ||
+      !make_map(&mk, a.k8, C::DK, k_rows, k_planes, C::DK, (uint64_t)k_rows * C::DK, C::SW, 128, qk_sw) ||
+      !make_map(&mv, a.v8t, k_rows, D, k_planes, k_rows, (uint64_t)k_rows * D, 128, D, CU_TENSOR_MAP_SWIZZLE_128B))
     return kStatusInvalid;
   AttnParams p;
   p.qs = a.qs;
@@ -523,7 +557,13 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.Hkv = a.Hkv;
   p.Sq = a.Sq;
   p.Skv = a.Skv;
-  p.nkb = (int)(skv_pad / kKvBlock);
+  p.nkb = varlen ? 0 : (int)(k_rows / kKvBlock);
+  p.cu_q = a.cu_q;
+  p.cu_k = a.cu_k;
+  p.cu_pad = a.cu_pad;
+  p.seg_ok = a.seg_ok;
+  p.total_q = a.total_q;
+  p.pad_total = a.pad_total;
   p.q_groups = (a.Sq + C::QT * 128 - 1) / (C::QT * 128);
   p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   p.out_f16 = a.out_dtype == 1;

@@ -97,6 +97,45 @@ static Workspace carve(void* base, int B, int H, int Hkv, int Sq, int Skv, int D
   return w;
 }
 
+// Workspace of the varlen entry point: quantised tensors in packed form plus the padded key offsets.
+struct VarlenWorkspace {
+  int8_t* q8;     // [H, total_q, DK]
+  float* qs;      // [H, total_q]
+  int8_t* k8;     // [Hkv, pad_total, DK]
+  float* ks;      // [Hkv, pad_total / 32]
+  uint8_t* v8t;   // [Hkv, D, pad_total]
+  float* vs;      // [nseq, Hkv, D]
+  int* cu_pad;    // [nseq + 1]
+  int* ok;        // offset check passed
+  int64_t pad_total;
+  size_t bytes;
+};
+
+static VarlenWorkspace carve_varlen(void* base, int nseq, int H, int Hkv, int total_q, int total_k, int D) {
+  const size_t dk = (size_t)qk_row_bytes(D);
+  // every sequence pads its keys to a multiple of 32, so the packed padded length is at most this
+  const int64_t pad = kv_pad((int64_t)total_k + (int64_t)(kKvBlock - 1) * nseq);
+  size_t off = 0;
+  VarlenWorkspace w{};
+  char* c = static_cast<char*>(base);
+  auto take = [&](size_t n) {
+    char* p = c ? c + off : nullptr;
+    off += align256(n);
+    return p;
+  };
+  w.q8 = reinterpret_cast<int8_t*>(take((size_t)H * total_q * dk));
+  w.qs = reinterpret_cast<float*>(take((size_t)H * total_q * 4));
+  w.k8 = reinterpret_cast<int8_t*>(take((size_t)Hkv * pad * dk));
+  w.ks = reinterpret_cast<float*>(take((size_t)Hkv * (pad / kKvBlock) * 4));
+  w.v8t = reinterpret_cast<uint8_t*>(take((size_t)Hkv * D * pad));
+  w.vs = reinterpret_cast<float*>(take((size_t)nseq * Hkv * D * 4));
+  w.cu_pad = reinterpret_cast<int*>(take((size_t)(nseq + 1) * 4));
+  w.ok = reinterpret_cast<int*>(take(4));
+  w.pad_total = pad;
+  w.bytes = off;
+  return w;
+}
+
 // math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)
 static bool isclose_rel(double a, double b, double rel) {
   return std::fabs(a - b) <= rel * std::fmax(std::fabs(a), std::fabs(b));
@@ -208,6 +247,71 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
     rc = sage_attn_fwd(w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, out, dtype, B, H, Hkv, Sq, Skv, D, causal, osb, oss, osh,
                        lse, status, s);
   return rc;
+}
+
+size_t sage_varlen_workspace_bytes(int nseq, int H, int Hkv, int total_q, int total_k, int D) {
+  if (sage_qk_row_bytes(D) == 0 || nseq <= 0 || H <= 0 || Hkv <= 0 || total_q <= 0 || total_k < 0) return 0;
+  return carve_varlen(nullptr, nseq, H, Hkv, total_q, total_k, D).bytes;
+}
+
+int sage_attention_varlen(const void* q, const void* k, const void* v, int dtype, int nseq, int H, int Hkv, int D,
+                          const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k, int max_seqlen_q, int max_seqlen_k,
+                          int total_q, int total_k, int64_t qss, int64_t qsh, int64_t kss, int64_t ksh, int64_t vss,
+                          int64_t vsh, double sm_scale, int causal, void* out, int64_t oss, int64_t osh, float* lse,
+                          void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(dtype, nseq, total_q, H, D);
+  if (rc != SAGE_OK) return rc;
+  if (Hkv <= 0 || H % Hkv != 0 || total_k < 0 || max_seqlen_q <= 0 || max_seqlen_k < 0) {
+    set_error("heads %d / kv heads %d, total_k %d, max_seqlen_q %d, max_seqlen_k %d", H, Hkv, total_k, max_seqlen_q,
+              max_seqlen_k);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (cu_seqlens_q == nullptr || cu_seqlens_k == nullptr) {
+    set_error("cu_seqlens_q / cu_seqlens_k must be device arrays of nseq + 1 int32");
+    return SAGE_ERR_INVALID;
+  }
+  rc = check_input(q, 0, qss, qsh, "q");
+  if (rc == SAGE_OK) rc = check_input(k, 0, kss, ksh, "k");
+  if (rc == SAGE_OK) rc = check_input(v, 0, vss, vsh, "v");
+  if (rc == SAGE_OK) rc = check_input(out, 0, oss, osh, "out");
+  if (rc != SAGE_OK) return rc;
+  const size_t need = sage_varlen_workspace_bytes(nseq, H, Hkv, total_q, total_k, D);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+    set_error("workspace of %zu bytes (16-byte aligned) required, got %zu", need, workspace_bytes);
+    return SAGE_ERR_INVALID;
+  }
+  const VarlenWorkspace w = carve_varlen(workspace, nseq, H, Hkv, total_q, total_k, D);
+  float fold = 1.0f;
+  if (sm_scale > 0.0 && !isclose_rel(sm_scale, 1.0 / std::sqrt((double)D), 1e-6))
+    fold = (float)(sm_scale * std::sqrt((double)D));
+  int* word = status != nullptr ? status : default_status_word();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Segs sg;
+  sg.cu = cu_seqlens_k;
+  sg.cu_pad = w.cu_pad;
+  sg.ok = w.ok;
+  sg.pad_total = w.pad_total;
+  const int grid_k = max_seqlen_k > 0 ? max_seqlen_k : 1;  // grid sizing only; each block reads its own length
+  rc = launch_varlen_offsets(cu_seqlens_q, cu_seqlens_k, nseq, total_q, total_k, max_seqlen_q, max_seqlen_k,
+                             w.cu_pad, w.ok, word, s);
+  if (rc == SAGE_OK) rc = launch_v_amax(v, dtype, nseq, grid_k, Hkv, D, Strides3{0, vss, vsh}, w.vs, s, sg);
+  if (rc == SAGE_OK)
+    rc = launch_quant_q(q, dtype, 1, total_q, H, D, Strides3{0, qss, qsh}, fold, w.q8, w.qs, s);
+  if (rc == SAGE_OK)
+    rc = launch_quant_kv(k, v, dtype, nseq, grid_k, Hkv, D, Strides3{0, kss, ksh}, Strides3{0, vss, vsh}, w.vs, w.k8,
+                         w.ks, w.v8t, s, sg);
+  if (rc == SAGE_OK) rc = launch_varlen_vtail(w.v8t, Hkv, D, w.pad_total, w.cu_pad, nseq, w.ok, s);
+  if (rc != SAGE_OK) return rc;
+  AttnArgs a{w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, out, dtype, Strides3{0, oss, osh}, lse, word, nseq, H, Hkv,
+             max_seqlen_q, grid_k, D, causal ? 1 : 0};
+  a.cu_q = cu_seqlens_q;
+  a.cu_k = cu_seqlens_k;
+  a.cu_pad = w.cu_pad;
+  a.seg_ok = w.ok;
+  a.total_q = total_q;
+  a.pad_total = w.pad_total;
+  return launch_attention(a, s);
 }
 
 int sage_status_sync(int* status, void* stream) {

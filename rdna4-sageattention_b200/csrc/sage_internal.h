@@ -31,11 +31,35 @@ struct Strides3 {
 
 void set_error(const char* fmt, ...);
 
-int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream);
+// Packed variable-length batches (the varlen entry point): sequence i owns tokens [cu[i], cu[i+1]) of
+// the packed (token, head, channel) tensors, whose batch stride is unused.  Its keys start at row
+// cu_pad[i] (a multiple of 32) of the quantised K / V, whose rows per head number pad_total.  `ok`
+// is set to 1 by the offset check (launch_varlen_offsets); the varlen kernels read and write nothing
+// while it is 0.  cu == nullptr means dense batches.
+struct Segs {
+  const int* cu = nullptr;
+  const int* cu_pad = nullptr;
+  const int* ok = nullptr;
+  int64_t pad_total = 0;
+};
+
+// Checks cu_q / cu_k (start at 0, non-decreasing, end at total_q / total_k, no sequence longer than
+// max_q / max_k) and writes cu_pad[0..nseq] = running sum of ceil(len_k / 32) * 32 and *ok; an
+// inconsistent table stores SAGE_ERR_INVALID into *status and leaves *ok = 0.
+int launch_varlen_offsets(const int* cu_q, const int* cu_k, int nseq, int total_q, int total_k, int max_q, int max_k,
+                          int* cu_pad, int* ok, int* status, cudaStream_t stream);
+
+// Zeroes V^T columns [cu_pad[nseq], cu_pad[nseq] + 128) of every (kv head, channel) row (within pad_total).
+int launch_varlen_vtail(uint8_t* v8t, int Hkv, int D, int64_t pad_total, const int* cu_pad, int nseq, const int* ok,
+                        cudaStream_t stream);
+int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream,
+                  const Segs& sg = Segs());
 int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides3 st, float fold, int8_t* q8,
                    float* qs, cudaStream_t stream);
+// Varlen (sg.cu set): B is the number of sequences and S the longest key length.
 int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
-                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream);
+                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream,
+                    const Segs& sg = Segs());
 
 struct AttnArgs {
   const int8_t* q8;
@@ -51,6 +75,13 @@ struct AttnArgs {
   int* status;       // device status word or null
   int B, H, Hkv, Sq, Skv, D;
   int causal;
+  // varlen: B = number of sequences, Sq = longest query length; q8 / qs are [H, total_q] packed
+  const int* cu_q = nullptr;
+  const int* cu_k = nullptr;
+  const int* cu_pad = nullptr;
+  const int* seg_ok = nullptr;
+  int total_q = 0;
+  int64_t pad_total = 0;
 };
 int launch_attention(const AttnArgs& a, cudaStream_t stream);
 // Query rows one attention CTA owns for head dim D (the grid is B * H * ceil(Sq / rows)).

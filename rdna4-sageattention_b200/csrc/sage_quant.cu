@@ -174,17 +174,33 @@ __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x,
 // ------------------------------------------------------------------------------------------------
 // K + V: one thread per key row; a warp is one 32-key K scale block
 // ------------------------------------------------------------------------------------------------
-template <int D, typename T>
+template <int D, typename T, bool VARLEN>
 __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
                                                          int H, Strides3 sk, Strides3 sv, const float* __restrict__ vs,
                                                          int8_t* __restrict__ k8, float* __restrict__ ks,
-                                                         uint8_t* __restrict__ v8t) {
+                                                         uint8_t* __restrict__ v8t, Segs sg) {
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
-  const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
   const int bh = blockIdx.y;
   const int b = bh / H;
   const int h = bh - b * H;
   const int s = blockIdx.x * kRows + threadIdx.x;
+  // this block's sequence: dense batch b, or packed sequence b (tokens from t0, output rows from o0)
+  int64_t src_b = b, t0 = 0;  // source batch index and first token
+  int64_t o0, pitch, vbase;   // first k8 row of this (batch, head), rows per head, first v8t byte
+  if constexpr (VARLEN) {
+    if (*sg.ok == 0) return;  // offsets failed the check
+    src_b = 0;
+    t0 = sg.cu[b];
+    S = sg.cu[b + 1] - (int)t0;
+    pitch = sg.pad_total;
+    o0 = (int64_t)h * pitch + sg.cu_pad[b];
+    vbase = (int64_t)h * D * pitch + sg.cu_pad[b];
+  } else {
+    pitch = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
+    o0 = (int64_t)bh * pitch;
+    vbase = (int64_t)bh * D * pitch;
+  }
+  const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
   __shared__ float fac[D];   // per-channel V factor 448 / max(amax, 1e-30) (sage_quant.py:68-69)
   for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
   __syncthreads();
@@ -192,19 +208,21 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
   const bool valid = s < S;        // real key (rows in [S, spad) are zero padding)
   const bool inpad = s < spad;     // row exists in the padded tensors
   const int lane = threadIdx.x & 31;
+  const int64_t orow = o0 + s;     // output row (a multiple of 32 starts every scale block)
 
   // K: codes and the block scale (warp max of the 32 rows' amax)
-  const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h;
-  const float kscale = quant_row<D, T>(krow, valid, k8 + ((int64_t)bh * spad + s) * DK, inpad, [](float a) {
+  const T* krow = k + src_b * sk.b + (t0 + (valid ? s : 0)) * sk.s + (int64_t)h * sk.h;
+  const float kscale = quant_row<D, T>(krow, valid, k8 + orow * DK, inpad, [](float a) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
   });
-  if (lane == 0) ks[(int64_t)bh * (spad / kKvBlock) + s / kKvBlock] = kscale;
+  if (lane == 0) ks[orow / kKvBlock] = kscale;
 
   // V: per-channel scale to e4m3; channel c of this key goes to v8t[b, h, c, s] (32 lanes = 32
   // consecutive bytes of each channel row)
   if (!inpad) return;
-  const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h;
-  uint8_t* vout = v8t + (int64_t)bh * D * spad + s;
+  const T* vrow = v + src_b * sv.b + (t0 + (valid ? s : 0)) * sv.s + (int64_t)h * sv.h;
+  const int64_t spitch = pitch;
+  uint8_t* vout = v8t + vbase + s;
 #pragma unroll 2
   for (int c = 0; c < D; c += 8) {
     const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(vrow + c)) : make_uint4(0, 0, 0, 0);
@@ -214,8 +232,8 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
       const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
       const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
       const uint16_t pk = pack_e4m3x2(y0, y1);
-      vout[(int64_t)(c + kx) * spad] = (uint8_t)(pk & 0xff);
-      vout[(int64_t)(c + kx + 1) * spad] = (uint8_t)(pk >> 8);
+      vout[(int64_t)(c + kx) * spitch] = (uint8_t)(pk & 0xff);
+      vout[(int64_t)(c + kx + 1) * spitch] = (uint8_t)(pk >> 8);
     }
   }
 }
@@ -223,9 +241,9 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
 // ------------------------------------------------------------------------------------------------
 // V channel amax (vs must be zero on entry; max via the order of non-negative float bit patterns)
 // ------------------------------------------------------------------------------------------------
-template <int D, typename T>
+template <int D, typename T, bool VARLEN>
 __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, int S, int H, Strides3 st,
-                                                     int rows_per_cta, float* __restrict__ vs) {
+                                                     int rows_per_cta, float* __restrict__ vs, Segs sg) {
   constexpr int G = D / 8;           // 8-channel groups per row
   constexpr int RSTEP = 256 / G;     // rows covered per pass
   __shared__ float red[256][8];
@@ -234,11 +252,17 @@ __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, in
   const int h = bh - b * H;
   const int g = threadIdx.x % G;
   const int r0 = threadIdx.x / G;
+  int64_t first = (int64_t)b * st.b;  // element offset of this batch's first token
+  if constexpr (VARLEN) {
+    if (*sg.ok == 0) return;  // offsets failed the check
+    first = (int64_t)sg.cu[b] * st.s;
+    S = sg.cu[b + 1] - sg.cu[b];
+  }
   const int s_begin = blockIdx.x * rows_per_cta;
   const int s_end = min(S, s_begin + rows_per_cta);
   float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (r0 < RSTEP) {
-    const T* base = v + (int64_t)b * st.b + (int64_t)h * st.h + g * 8;
+    const T* base = v + first + (int64_t)h * st.h + g * 8;
     for (int s = s_begin + r0; s < s_end; s += RSTEP) {
       const uint4 raw = __ldg(reinterpret_cast<const uint4*>(base + (int64_t)s * st.s));
       const T* e = reinterpret_cast<const T*>(&raw);
@@ -284,22 +308,27 @@ static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold
 
 template <int D, typename T>
 static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
-                      int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream) {
-  const int spad = (int)kv_pad(S);
+                      int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
+  const int spad = (int)kv_pad(S);  // varlen: S is the longest sequence
   dim3 grid((spad + kRows - 1) / kRows, B * H);
-  quant_kv_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), S,
-                                                    H, sk, sv, vs, k8, ks, v8t);
+  const T* kp = reinterpret_cast<const T*>(k);
+  const T* vp = reinterpret_cast<const T*>(v);
+  if (sg.cu != nullptr)
+    quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg);
+  else
+    quant_kv_kernel<D, T, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg);
   return check_launch("quant_kv");
 }
 
 template <int D, typename T>
-static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, cudaStream_t stream) {
+static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, cudaStream_t stream, const Segs& sg) {
   cudaError_t e = cudaMemsetAsync(vs, 0, sizeof(float) * (size_t)B * H * D, stream);
   if (e != cudaSuccess) {
     set_error("v_amax memset: %s", cudaGetErrorString(e));
     return kStatusLaunch;
   }
   // enough CTAs to fill the GPU several times over, each covering a contiguous run of rows
+  // (varlen: S is the longest sequence; blocks past a shorter sequence's end read nothing)
   const int bh = B * H;
   int chunks = (S + 511) / 512;
   const int want = (148 * 8 + bh - 1) / bh;
@@ -307,8 +336,55 @@ static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, 
   if (chunks < 1) chunks = 1;
   const int rows_per_cta = (S + chunks - 1) / chunks;
   dim3 grid(chunks, bh);
-  v_amax_kernel<D, T><<<grid, 256, 0, stream>>>(reinterpret_cast<const T*>(v), S, H, st, rows_per_cta, vs);
+  const T* vp = reinterpret_cast<const T*>(v);
+  if (sg.cu != nullptr)
+    v_amax_kernel<D, T, true><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg);
+  else
+    v_amax_kernel<D, T, false><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg);
   return check_launch("v_amax");
+}
+
+// ------------------------------------------------------------------------------------------------
+// varlen offsets: check the cumulative sequence tables and derive the padded key offsets
+// ------------------------------------------------------------------------------------------------
+__global__ void varlen_offsets_kernel(const int* __restrict__ cu_q, const int* __restrict__ cu_k, int nseq,
+                                      int total_q, int total_k, int max_q, int max_k, int* __restrict__ cu_pad,
+                                      int* __restrict__ ok, int* __restrict__ status) {
+  // one thread: the tables are short (one entry per sequence) and read once
+  if (threadIdx.x != 0) return;
+  bool good = cu_q[0] == 0 && cu_k[0] == 0 && cu_q[nseq] == total_q && cu_k[nseq] == total_k;
+  int pad = 0;
+  cu_pad[0] = 0;
+  for (int i = 0; i < nseq && good; ++i) {
+    const int lq = cu_q[i + 1] - cu_q[i];
+    const int lk = cu_k[i + 1] - cu_k[i];
+    good = lq >= 0 && lk >= 0 && lq <= max_q && lk <= max_k;
+    pad += (lk + kKvBlock - 1) / kKvBlock * kKvBlock;
+    cu_pad[i + 1] = pad;
+  }
+  *ok = good ? 1 : 0;
+  if (!good) atomicCAS(status, 0, kStatusInvalid);
+}
+
+// The last key tile of the last sequence reads up to 127 key columns of V^T past cu_pad[nseq]; its p is 0
+// there, and 0 * NaN would still poison O, so those columns (within pad_total) are zeroed.
+__global__ void varlen_vtail_kernel(uint8_t* __restrict__ v8t, int64_t pad_total, const int* __restrict__ cu_pad,
+                                    int nseq, const int* __restrict__ ok) {
+  if (*ok == 0) return;
+  const int64_t col = (int64_t)cu_pad[nseq] + threadIdx.x;
+  if (col < pad_total) v8t[(int64_t)blockIdx.x * pad_total + col] = 0;
+}
+
+int launch_varlen_vtail(uint8_t* v8t, int Hkv, int D, int64_t pad_total, const int* cu_pad, int nseq, const int* ok,
+                        cudaStream_t stream) {
+  varlen_vtail_kernel<<<Hkv * D, 128, 0, stream>>>(v8t, pad_total, cu_pad, nseq, ok);
+  return check_launch("varlen_vtail");
+}
+
+int launch_varlen_offsets(const int* cu_q, const int* cu_k, int nseq, int total_q, int total_k, int max_q, int max_k,
+                          int* cu_pad, int* ok, int* status, cudaStream_t stream) {
+  varlen_offsets_kernel<<<1, 32, 0, stream>>>(cu_q, cu_k, nseq, total_q, total_k, max_q, max_k, cu_pad, ok, status);
+  return check_launch("varlen_offsets");
 }
 
 #define SAGE_DISPATCH_D(D_, FN, ...)                                                              \
@@ -320,8 +396,9 @@ static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, 
     default: set_error("head_dim %d is not supported (64, 96, 128, 256)", D_); return kStatusUnsupported; \
   }
 
-int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream) {
-  SAGE_DISPATCH_D(D, v_amax_t, v, B, S, H, st, vs, stream)
+int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3 st, float* vs, cudaStream_t stream,
+                  const Segs& sg) {
+  SAGE_DISPATCH_D(D, v_amax_t, v, B, S, H, st, vs, stream, sg)
 }
 
 int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides3 st, float fold, int8_t* q8,
@@ -330,8 +407,8 @@ int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides
 }
 
 int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
-                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream) {
-  SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream)
+                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
+  SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream, sg)
 }
 
 }  // namespace sage

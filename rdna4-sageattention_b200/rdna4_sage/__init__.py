@@ -12,9 +12,11 @@ import torch
 from torch.nn.attention.bias import causal_lower_right
 
 from . import ops
-from ._attention import ARCHS, HEAD_DIMS, Unsupported, attention_host, check_supported, device_arch
+from ._attention import (ARCHS, HEAD_DIMS, Unsupported, attention_host, check_supported, check_supported_varlen,
+                         device_arch)
 
-__all__ = ["sageattn", "attention", "attention_host", "is_available", "Unsupported", "ARCHS", "HEAD_DIMS"]
+__all__ = ["sageattn", "attention", "attention_varlen", "attention_host", "is_available", "Unsupported", "ARCHS",
+           "HEAD_DIMS"]
 __version__ = "0.2.1+b200"
 
 # The C binding behind F.scaled_dot_product_attention. Apps replace F.scaled_dot_product_attention with
@@ -39,6 +41,14 @@ def attention(q, k, v, tensor_layout="HND", sm_scale=None, is_causal=False):
     Causal attention needs q_len == kv_len."""
     out = ops.attention(q, k, v, tensor_layout, float(sm_scale or 0.0), bool(is_causal))
     return out.transpose(1, 2) if tensor_layout == "HND" else out
+
+
+def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, sm_scale=None,
+                     is_causal=False):
+    """Packed variable-length attention in one kernel pipeline (q [total_q, H, D], k / v [total_k, Hkv, D],
+    int32 cu_seqlens on the GPU); raises Unsupported if it cannot run.  Returns [total_q, H, D]."""
+    return ops.attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, int(max_seqlen_q), int(max_seqlen_k),
+                                float(sm_scale or 0.0), bool(is_causal))
 
 
 def _sdpa(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask):

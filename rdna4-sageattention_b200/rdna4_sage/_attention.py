@@ -135,6 +135,70 @@ def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=
     return (out, lse) if return_lse else out
 
 
+def _th(t: torch.Tensor):
+    """(token, head) element strides of a packed [total, heads, D] tensor, made 16-byte aligned if needed."""
+    if t.stride(-1) != 1 or t.data_ptr() % 16 or t.stride(0) % 8 or t.stride(1) % 8:
+        t = t.contiguous()
+    return t, (t.stride(0), t.stride(1))
+
+
+def check_supported_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k):
+    """Raise Unsupported if the packed variable-length kernels cannot run these inputs."""
+    if not (q.is_cuda and k.device == q.device and v.device == q.device):
+        raise Unsupported("tensors must be on one CUDA GPU")
+    _check_arch(q.device)
+    if q.dtype not in DTYPES or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise Unsupported(f"dtype {q.dtype}/{k.dtype}/{v.dtype} (fp16 or bf16 required)")
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise Unsupported("packed [total, heads, head_dim] tensors required")
+    hd = q.shape[-1]
+    if hd not in HEAD_DIMS or k.shape[-1] != hd or v.shape[-1] != hd:
+        raise Unsupported(f"head_dim {hd} (supported {HEAD_DIMS})")
+    if k.shape[:2] != v.shape[:2] or q.shape[1] % k.shape[1]:
+        raise Unsupported("k / v shapes differ or heads not a multiple of kv heads")
+    if q.shape[0] == 0 or max(q.numel(), k.numel()) > _I32_MAX:
+        raise Unsupported("empty or too large for 32-bit indexing")
+    for cu in (cu_seqlens_q, cu_seqlens_k):
+        if cu.dim() != 1 or cu.dtype != torch.int32 or cu.device != q.device:
+            raise Unsupported("cu_seqlens must be 1-D int32 tensors on the GPU")
+    if cu_seqlens_q.numel() != cu_seqlens_k.numel() or cu_seqlens_q.numel() < 2:
+        raise Unsupported("cu_seqlens_q and cu_seqlens_k need the same batch + 1 entries")
+
+
+def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, sm_scale=None,
+                     is_causal=False, return_lse=False):
+    """Packed variable-length attention in one call with no host synchronisation: q [total_q, H, D],
+    k / v [total_k, Hkv, D], cu_seqlens int32 [batch + 1] on the GPU.  Returns [total_q, H, D] in q's dtype
+    and with return_lse also the [H, total_q] fp32 log-sum-exp.  Every sequence's rows equal those of
+    attention() on that sequence alone.  An inconsistent cu_seqlens table (or a max_seqlen below a length)
+    is caught on the device: the status word then holds "invalid argument" (check_status raises) and the
+    output is left unwritten."""
+    check_supported_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k)
+    L = _lib.lib()
+    dev = q.device
+    total_q, H, D = q.shape
+    total_k, Hkv = k.shape[0], k.shape[1]
+    nseq = cu_seqlens_q.numel() - 1
+    q, sq_ = _th(q)
+    k, sk_ = _th(k)
+    v, sv_ = _th(v)
+    cq, ck = cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous()
+    out = torch.empty((total_q, H, D), device=dev, dtype=q.dtype)
+    lse = torch.empty((H, total_q), device=dev, dtype=torch.float32) if return_lse else None
+    ws_bytes = L.sage_varlen_workspace_bytes(nseq, H, Hkv, total_q, total_k, D)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = L.sage_attention_varlen(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[q.dtype], nseq, H, Hkv, D,
+                                 cq.data_ptr(), ck.data_ptr(), int(max_seqlen_q), int(max_seqlen_k), total_q, total_k,
+                                 *sq_, *sk_, *sv_, float(sm_scale or 0.0), int(bool(is_causal)), out.data_ptr(),
+                                 out.stride(0), out.stride(1), lse.data_ptr() if lse is not None else None,
+                                 ws.data_ptr(), ws_bytes, status_word(dev).data_ptr(), stream)
+    _lib.check(rc, "sage_attention_varlen")
+    if _CHECK:
+        check_status(dev)
+    return (out, lse) if return_lse else out
+
+
 def _bsh_host(t: torch.Tensor, layout: str):
     """(batch, seq, head) element strides of a host tensor; the channel axis must be contiguous."""
     if t.stride(-1) != 1:

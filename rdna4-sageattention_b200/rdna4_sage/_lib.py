@@ -48,6 +48,10 @@ SIGNATURES = {
     "sage_attention_static": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,
                                      _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,
                                      _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
+    "sage_varlen_workspace_bytes": (_c_sz, [_c_i] * 6),
+    "sage_attention_varlen": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_p, _c_p, _c_i, _c_i, _c_i,
+                                     _c_i, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p, _c_i64,
+                                     _c_i64, _c_p, _c_p, _c_sz, _c_p, _c_p]),
     "sage_host_heads_per_chunk": (_c_i, [_c_i] * 7),
     "sage_host_workspace_bytes": (_c_sz, [_c_i] * 7),
     "sage_attention_host": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,

@@ -98,7 +98,21 @@ def sageattn_varlen(
     smooth_k: bool = True,
     **kwargs: Any,
 ) -> torch.Tensor:
-    """Packed variable-length attention: q [total_q, H, D], k / v [total_k, Hkv, D], cu_seqlens [batch + 1]."""
+    """Packed variable-length attention: q [total_q, H, D], k / v [total_k, Hkv, D], cu_seqlens [batch + 1].
+
+    On a B200 with supported inputs and enough work (total_q * max_seqlen_k * H >= rdna4_sage.MIN_WORK and
+    max_seqlen_k >= rdna4_sage.MIN_KV) the whole batch runs as one kernel pipeline with no host
+    synchronisation (rdna4_sage.attention_varlen); every sequence's rows equal a dense call on it.
+    Otherwise each sequence goes through sageattn in turn, as the reference shim does (core.py:66-89)."""
+    if kwargs.get("attn_mask") is None and max_seqlen_k >= rdna4_sage.MIN_KV and \
+            q.shape[0] * max_seqlen_k * q.shape[1] >= rdna4_sage.MIN_WORK:
+        try:
+            rdna4_sage.check_supported_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k)
+        except rdna4_sage.Unsupported:
+            pass
+        else:
+            return rdna4_sage.attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
+                                               sm_scale=sm_scale, is_causal=is_causal)
     cq = cu_seqlens_q.tolist()
     ck = cu_seqlens_k.tolist()
     out = torch.empty_like(q)

@@ -137,6 +137,12 @@ int sage_attention_host(const void* q, const void* k, const void* v, int dtype, 
                         int64_t oss, int64_t osh, float* lse, int heads_per_chunk, void* workspace,
                         size_t workspace_bytes, int* status, void* stream);
 
+/* Failure-path self test (no counterpart in the reference): enqueues a kernel whose single wait is on a
+ * barrier that nothing completes, bounded by limit_ms (1..2000) instead of the pipeline's 2 s.  When the
+ * work on `stream` is done, the status word (NULL = the library's own) holds SAGE_ERR_TIMEOUT, exactly as
+ * after a stalled pipeline stage, and the context is still usable. */
+int sage_selftest_wait_timeout(int* status, int limit_ms, void* stream);
+
 /* Synchronise `stream`, read and clear a status word (NULL = the library's own word on the current
  * device); returns the code it held (SAGE_OK when no kernel reported an error). */
 int sage_status_sync(int* status, void* stream);

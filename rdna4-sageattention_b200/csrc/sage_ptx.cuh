@@ -76,6 +76,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 struct WaitCtx {
   volatile int* cta_abort;   // shared memory: set when any wait of this CTA gave up
   int* status;               // global memory: first error code of the launch (0 = ok)
+  uint64_t limit_ns = kWaitLimitNs;
 };
 
 __device__ __forceinline__ bool aborted(const WaitCtx& w) {
@@ -95,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   while (!mbar_try_wait(bar, parity)) {
     if ((++n & 63u) == 0) {
       if (aborted(w)) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > w.limit_ns) {
         raise_timeout(w);
         return false;
       }

@@ -1,0 +1,49 @@
+// sage_selftest_wait_timeout: runs the kernels' bounded-wait failure path on purpose.  One thread waits on
+// an mbarrier that nothing arrives at, through the same mbar_wait the pipeline kernels use, with a short
+// limit; the wait gives up, records SAGE_ERR_TIMEOUT in the status word and the kernel returns normally,
+// so the CUDA context stays usable.  This is how the failure detection is tested without faulting a GPU.
+#include "../../include/sage_b200.h"
+#include "sage_internal.h"
+#include "sage_ptx.cuh"
+
+namespace sage {
+
+__global__ void wait_timeout_kernel(int* status, uint64_t limit_ns, int* gave_up) {
+  __shared__ uint64_t bar;
+  __shared__ int cta_abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);  // expects one arrival; none comes
+    cta_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    WaitCtx wc{&cta_abort, status, limit_ns};
+    const bool ok = mbar_wait(&bar, 0, wc);
+    if (gave_up != nullptr) *gave_up = ok ? 0 : 1;
+  }
+}
+
+}  // namespace sage
+
+using namespace sage;
+
+extern "C" int sage_selftest_wait_timeout(int* status, int limit_ms, void* stream) {
+  if (limit_ms < 1 || limit_ms > 2000) {
+    set_error("limit_ms %d (1..2000)", limit_ms);
+    return SAGE_ERR_INVALID;
+  }
+  int* word = status != nullptr ? status : default_status_word();
+  if (word == nullptr) {
+    set_error("no status word on this device");
+    return SAGE_ERR_LAUNCH;
+  }
+  wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(word, (uint64_t)limit_ms * 1000000ull,
+                                                                        nullptr);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("selftest launch: %s", cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  }
+  return SAGE_OK;
+}

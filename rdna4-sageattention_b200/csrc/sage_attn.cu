@@ -328,14 +328,14 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         const int st1 = (j + 1) % NST;
         const uint32_t ph1 = ((j + 1) / NST) & 1;
         if (QT == 2) {
-          if (!mbar_wait(&v_full[st], ph, wc) || !mbar_wait(&p_full[0], j & 1, wc)) break;
+          // V(j) and K(j+1) land long before P_0(j): wait for them first, so that nothing but the P wait
+          // sits between the softmax announcing P and the tensor core receiving PV and the next QK^T
+          if (!mbar_wait(&v_full[st], ph, wc)) break;
+          if (more && !mbar_wait(&k_full[st1], ph1, wc)) break;
+          if (!mbar_wait(&p_full[0], j & 1, wc)) break;
           tc_fence_after();
           issue_pv(j, 0, 0);
-          if (more) {
-            if (!mbar_wait(&k_full[st1], ph1, wc)) break;
-            tc_fence_after();
-            issue_s(j + 1, 0, 0);
-          }
+          if (more) issue_s(j + 1, 0, 0);
           if (!mbar_wait(&p_full[1], j & 1, wc)) break;
           tc_fence_after();
           issue_pv(j, 1, 1);

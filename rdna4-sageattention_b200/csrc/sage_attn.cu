@@ -79,8 +79,8 @@ struct AttnCfg {
   // registers per thread at launch (the launch bound gives 65536 / 384 rounded down to 8) and after
   // the rebalance; the shares must add up to exactly what the CTA was launched with
   static constexpr int REGS_LAUNCH = 168;
-  static constexpr int REGS_SOFTMAX = 200;
-  static constexpr int REGS_OTHER = 104;
+  static constexpr int REGS_SOFTMAX = 216;
+  static constexpr int REGS_OTHER = 72;
   static_assert(!REBALANCE || 2 * 128 * REGS_SOFTMAX + 128 * REGS_OTHER == THREADS * REGS_LAUNCH,
                 "setmaxnreg shares must sum to the launch allocation");
   static constexpr int O_COL = 256;

@@ -32,17 +32,30 @@ __device__ __forceinline__ float to_f32<__half>(__half v) {
 
 // One butterfly stage of the Walsh-Hadamard transform (pairs LEN apart), then the next stage.  The
 // stages are template-recursive so every index is a compile-time constant and x stays in registers.
+// From LEN = 2 on, neighbouring butterflies run as packed f32x2 operations (a + b, and a - b as
+// fma(b, -1, a)); each lane rounds exactly as the scalar add / subtract.
 template <int N, int LEN>
 __device__ __forceinline__ void fwht_stage(float* x) {
   if constexpr (LEN < N) {
+    if constexpr (LEN == 1) {
 #pragma unroll
-    for (int i = 0; i < N; i += 2 * LEN) {
-#pragma unroll
-      for (int j = i; j < i + LEN; ++j) {
+      for (int j = 0; j < N; j += 2) {
         const float a = x[j];
-        const float b = x[j + LEN];
+        const float b = x[j + 1];
         x[j] = a + b;
-        x[j + LEN] = a - b;
+        x[j + 1] = a - b;
+      }
+    } else {
+      const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+#pragma unroll
+      for (int i = 0; i < N; i += 2 * LEN) {
+#pragma unroll
+        for (int j = i; j < i + LEN; j += 2) {
+          const uint64_t a = f2_pack(x[j], x[j + 1]);
+          const uint64_t b = f2_pack(x[j + LEN], x[j + LEN + 1]);
+          f2_unpack(f2_add(a, b), x[j], x[j + 1]);
+          f2_unpack(f2_fma(b, neg1, a), x[j + LEN], x[j + LEN + 1]);
+        }
       }
     }
     fwht_stage<N, 2 * LEN>(x);
@@ -56,19 +69,14 @@ __device__ __forceinline__ void fwht(float* x) {
 }
 
 // trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32 (the reference's
-// rounding, kernel_build/sage_quant.py:44,65).  `rcp` is the correctly rounded 1/scale.  x * rcp is within
-// two ulps of the IEEE quotient, so it gives the same code unless y +- 0.5 lies within a few ulps of an
-// integer; those rare elements are recomputed with the IEEE division.
+// rounding, kernel_build/sage_quant.py:44,65).  y is the correctly rounded quotient from the correctly
+// rounded reciprocal `rcp` and one residual correction (Markstein's division step: q0 = x * rcp,
+// e = fma(-q0, scale, x), y = fma(e, rcp, q0)), so no element needs a second, IEEE division.
 __device__ __forceinline__ int quant_code(float x, float scale, float rcp) {
-  float y = x * rcp;
-  float t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
-  const float at = fabsf(t);
-  const float fr = at - truncf(at);
-  if (fr < 1e-4f || fr > 1.0f - 1e-4f) {
-    y = __fdiv_rn(x, scale);
-    t = y >= 0.f ? __fadd_rn(y, 0.5f) : __fsub_rn(y, 0.5f);
-  }
-  return __float2int_rz(t);
+  const float q0 = __fmul_rn(x, rcp);
+  const float e = __fmaf_rn(-q0, scale, x);
+  const float y = __fmaf_rn(e, rcp, q0);
+  return __float2int_rz(__fadd_rn(y, copysignf(0.5f, y)));
 }
 
 constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)

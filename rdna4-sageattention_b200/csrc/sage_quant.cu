@@ -68,17 +68,6 @@ __device__ __forceinline__ void fwht(float* x) {
   fwht_stage<N, 1>(x);
 }
 
-// trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in IEEE fp32 (the reference's
-// rounding, kernel_build/sage_quant.py:44,65).  y is the correctly rounded quotient from the correctly
-// rounded reciprocal `rcp` and one residual correction (Markstein's division step: q0 = x * rcp,
-// e = fma(-q0, scale, x), y = fma(e, rcp, q0)), so no element needs a second, IEEE division.
-__device__ __forceinline__ int quant_code(float x, float scale, float rcp) {
-  const float q0 = __fmul_rn(x, rcp);
-  const float e = __fmaf_rn(-q0, scale, x);
-  const float y = __fmaf_rn(e, rcp, q0);
-  return __float2int_rz(__fadd_rn(y, copysignf(0.5f, y)));
-}
-
 constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)
 
 // fp32 values of N consecutive channels of one token row read straight from global memory (16-byte
@@ -107,19 +96,37 @@ __device__ __forceinline__ float abs_max(const float* x) {
   return m;
 }
 
+// int8 codes of a packed pair: trunc(y + 0.5) for y >= 0, trunc(y - 0.5) otherwise, with y = x / scale in
+// IEEE fp32 (the reference's rounding, kernel_build/sage_quant.py:44,65).  y is the correctly rounded
+// quotient from the correctly rounded reciprocal and one residual correction (Markstein's division
+// step: q0 = x * rcp, e = fma(-q0, scale, x), y = fma(e, rcp, q0)), evaluated on both lanes at once.
+__device__ __forceinline__ void quant_code2(float x0, float x1, uint64_t scale2, uint64_t rcp2, int& c0, int& c1) {
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t q0 = f2_mul(x, rcp2);
+  float a0, a1;
+  f2_unpack(q0, a0, a1);
+  const uint64_t e = f2_fma(f2_pack(-a0, -a1), scale2, x);
+  float y0, y1;
+  f2_unpack(f2_fma(e, rcp2, q0), y0, y1);
+  float t0, t1;
+  f2_unpack(f2_add(f2_pack(y0, y1), f2_pack(copysignf(0.5f, y0), copysignf(0.5f, y1))), t0, t1);
+  c0 = __float2int_rz(t0);
+  c1 = __float2int_rz(t1);
+}
+
 // int8 codes of x[0..N) with `scale`, written as 16-byte stores to dst (global memory).
 template <int N>
 __device__ __forceinline__ void store_codes(const float* x, float scale, int8_t* dst) {
   const float rcp = __frcp_rn(scale);
+  const uint64_t scale2 = f2_pack(scale, scale), rcp2 = f2_pack(rcp, rcp);
 #pragma unroll
   for (int i = 0; i < N; i += 16) {
     uint32_t w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int c0 = quant_code(x[i + 4 * k + 0], scale, rcp);
-      const int c1 = quant_code(x[i + 4 * k + 1], scale, rcp);
-      const int c2 = quant_code(x[i + 4 * k + 2], scale, rcp);
-      const int c3 = quant_code(x[i + 4 * k + 3], scale, rcp);
+      int c0, c1, c2, c3;
+      quant_code2(x[i + 4 * k + 0], x[i + 4 * k + 1], scale2, rcp2, c0, c1);
+      quant_code2(x[i + 4 * k + 2], x[i + 4 * k + 3], scale2, rcp2, c2, c3);
       w[k] = (uint32_t)(c0 & 0xff) | ((uint32_t)(c1 & 0xff) << 8) | ((uint32_t)(c2 & 0xff) << 16) |
              ((uint32_t)(c3 & 0xff) << 24);
     }

@@ -135,6 +135,89 @@ def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=
     return (out, lse) if return_lse else out
 
 
+class QuantizedKV:
+    """K and V quantised once (int8 K with one scale per 32-key block, e4m3 V^T with per-channel scales) for
+    several attention calls on the same keys, e.g. cross-attention on a fixed text context.  Built by
+    quantize_kv(); used by attention_quantized_kv(), whose output equals attention() on the original K, V."""
+
+    def __init__(self, k8, ks, v8t, vs, B, Hkv, Skv, D, dtype):
+        self.k8, self.ks, self.v8t, self.vs = k8, ks, v8t, vs
+        self.B, self.Hkv, self.Skv, self.D, self.dtype = B, Hkv, Skv, D, dtype
+
+    @property
+    def device(self):
+        return self.k8.device
+
+
+def quantize_kv(k, v, tensor_layout="HND"):
+    """Quantise K and V (B, Hkv, Skv, D) for "HND" or (B, Skv, Hkv, D) for "NHD" into a QuantizedKV."""
+    if tensor_layout not in ("HND", "NHD"):
+        raise Unsupported(f"layout {tensor_layout!r}")
+    if not (k.is_cuda and v.device == k.device):
+        raise Unsupported("tensors must be on one CUDA GPU")
+    _check_arch(k.device)
+    _check_shapes(k, k, v, tensor_layout, False)
+    L = _lib.lib()
+    if tensor_layout == "HND":
+        B, Hkv, Skv, D = k.shape
+    else:
+        B, Skv, Hkv, D = k.shape
+    if Skv == 0:
+        raise Unsupported("empty keys")
+    k, sk_ = _bsh(k, tensor_layout)
+    v, sv_ = _bsh(v, tensor_layout)
+    dev, dt = k.device, DTYPES[k.dtype]
+    spad = (Skv + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
+    dk = L.sage_qk_row_bytes(D)
+    vs = torch.empty((B, Hkv, D), device=dev, dtype=torch.float32)
+    k8 = torch.empty((B, Hkv, spad, dk), device=dev, dtype=torch.int8)
+    ks = torch.empty((B, Hkv, spad // KV_BLOCK), device=dev, dtype=torch.float32)
+    v8t = torch.empty((B, Hkv, D, spad), device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.sage_v_amax(v.data_ptr(), dt, B, Skv, Hkv, D, *sv_, vs.data_ptr(), stream), "sage_v_amax")
+    _lib.check(L.sage_quant_kv(k.data_ptr(), v.data_ptr(), dt, B, Skv, Hkv, D, *sk_, *sv_, vs.data_ptr(),
+                               k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(), stream), "sage_quant_kv")
+    return QuantizedKV(k8, ks, v8t, vs, B, Hkv, Skv, D, k.dtype)
+
+
+def attention_quantized_kv(q, kv, tensor_layout="HND", sm_scale=None, is_causal=False, return_lse=False):
+    """attention() with K and V already quantised by quantize_kv(): only Q is quantised per call.  Returns
+    (B, Sq, H, D) contiguous in q's dtype (and the (B, H, Sq) LSE with return_lse)."""
+    if tensor_layout not in ("HND", "NHD"):
+        raise Unsupported(f"layout {tensor_layout!r}")
+    if not (q.is_cuda and q.device == kv.device):
+        raise Unsupported("q must be on the GPU that holds the quantised K / V")
+    if q.dtype != kv.dtype or q.dim() != 4 or q.shape[-1] != kv.D:
+        raise Unsupported("q must match the quantised K / V in dtype and head_dim")
+    if tensor_layout == "HND":
+        B, H, Sq, D = q.shape
+    else:
+        B, Sq, H, D = q.shape
+    if B != kv.B or H % kv.Hkv or Sq == 0:
+        raise Unsupported(f"batch {B} / heads {H} do not fit the quantised K / V ({kv.B}, {kv.Hkv})")
+    if is_causal and Sq != kv.Skv:
+        raise Unsupported("causal attention needs q_len == kv_len")
+    L = _lib.lib()
+    dev = q.device
+    q, sq_ = _bsh(q, tensor_layout)
+    dk = L.sage_qk_row_bytes(D)
+    q8 = torch.empty((B, H, Sq, dk), device=dev, dtype=torch.int8)
+    qs = torch.empty((B, H, Sq), device=dev, dtype=torch.float32)
+    out = torch.empty((B, Sq, H, D), device=dev, dtype=q.dtype)
+    lse = torch.empty((B, H, Sq), device=dev, dtype=torch.float32) if return_lse else None
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.check(L.sage_quant_q(q.data_ptr(), DTYPES[q.dtype], B, Sq, H, D, *sq_, float(sm_fold(sm_scale, D)),
+                              q8.data_ptr(), qs.data_ptr(), stream), "sage_quant_q")
+    _lib.check(L.sage_attn_fwd(q8.data_ptr(), qs.data_ptr(), kv.k8.data_ptr(), kv.ks.data_ptr(), kv.v8t.data_ptr(),
+                               kv.vs.data_ptr(), out.data_ptr(), DTYPES[q.dtype], B, H, kv.Hkv, Sq, kv.Skv, D,
+                               int(bool(is_causal)), out.stride(0), out.stride(1), out.stride(2),
+                               lse.data_ptr() if lse is not None else None, status_word(dev).data_ptr(), stream),
+               "sage_attn_fwd")
+    if _CHECK:
+        check_status(dev)
+    return (out, lse) if return_lse else out
+
+
 def _th(t: torch.Tensor):
     """(token, head) element strides of a packed [total, heads, D] tensor, made 16-byte aligned if needed."""
     if t.stride(-1) != 1 or t.data_ptr() % 16 or t.stride(0) % 8 or t.stride(1) % 8:

@@ -69,6 +69,7 @@ __device__ __forceinline__ void fwht(float* x) {
 }
 
 constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)
+constexpr int kMaxGridY = 65535;  // (batch, head) planes per launch (the grid's y limit)
 
 // fp32 values of N consecutive channels of one token row read straight from global memory (16-byte
 // loads; the row's bytes are contiguous), rotated by the Walsh-Hadamard transform when `rot`.
@@ -171,9 +172,10 @@ __device__ __forceinline__ float quant_row(const T* __restrict__ row, bool valid
 // ------------------------------------------------------------------------------------------------
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
-                                                        float fold, int8_t* __restrict__ q8, float* __restrict__ qs) {
+                                                        float fold, int8_t* __restrict__ q8, float* __restrict__ qs,
+                                                        int bh0) {
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
-  const int bh = blockIdx.y;
+  const int bh = bh0 + (int)blockIdx.y;  // (batch, head) planes come in launches of at most 65535
   const int b = bh / H;
   const int h = bh - b * H;
   const int s = blockIdx.x * kRows + threadIdx.x;
@@ -193,9 +195,9 @@ template <int D, typename T, bool VARLEN>
 __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
                                                          int H, Strides3 sk, Strides3 sv, const float* __restrict__ vs,
                                                          int8_t* __restrict__ k8, float* __restrict__ ks,
-                                                         uint8_t* __restrict__ v8t, Segs sg) {
+                                                         uint8_t* __restrict__ v8t, Segs sg, int bh0) {
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
-  const int bh = blockIdx.y;
+  const int bh = bh0 + (int)blockIdx.y;  // (batch, head) planes come in launches of at most 65535
   const int b = bh / H;
   const int h = bh - b * H;
   const int s = blockIdx.x * kRows + threadIdx.x;
@@ -258,11 +260,11 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
 // ------------------------------------------------------------------------------------------------
 template <int D, typename T, bool VARLEN>
 __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, int S, int H, Strides3 st,
-                                                     int rows_per_cta, float* __restrict__ vs, Segs sg) {
+                                                     int rows_per_cta, float* __restrict__ vs, Segs sg, int bh0) {
   constexpr int G = D / 8;           // 8-channel groups per row
   constexpr int RSTEP = 256 / G;     // rows covered per pass
   __shared__ float red[256][8];
-  const int bh = blockIdx.y;
+  const int bh = bh0 + (int)blockIdx.y;  // (batch, head) planes come in launches of at most 65535
   const int b = bh / H;
   const int h = bh - b * H;
   const int g = threadIdx.x % G;
@@ -316,23 +318,29 @@ static int check_launch(const char* what) {
 template <int D, typename T>
 static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold, int8_t* q8, float* qs,
                      cudaStream_t stream) {
-  dim3 grid((S + kRows - 1) / kRows, B * H);
-  quant_q_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs);
-  return check_launch("quant_q");
+  for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
+    dim3 grid((S + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
+    quant_q_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs, bh0);
+    if (check_launch("quant_q") != kStatusOk) return kStatusLaunch;
+  }
+  return kStatusOk;
 }
 
 template <int D, typename T>
 static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
                       int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
   const int spad = (int)kv_pad(S);  // varlen: S is the longest sequence
-  dim3 grid((spad + kRows - 1) / kRows, B * H);
   const T* kp = reinterpret_cast<const T*>(k);
   const T* vp = reinterpret_cast<const T*>(v);
-  if (sg.cu != nullptr)
-    quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg);
-  else
-    quant_kv_kernel<D, T, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg);
-  return check_launch("quant_kv");
+  for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
+    dim3 grid((spad + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
+    if (sg.cu != nullptr)
+      quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
+    else
+      quant_kv_kernel<D, T, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
+    if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
+  }
+  return kStatusOk;
 }
 
 template <int D, typename T>
@@ -350,13 +358,16 @@ static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, 
   if (chunks > want) chunks = want;
   if (chunks < 1) chunks = 1;
   const int rows_per_cta = (S + chunks - 1) / chunks;
-  dim3 grid(chunks, bh);
   const T* vp = reinterpret_cast<const T*>(v);
-  if (sg.cu != nullptr)
-    v_amax_kernel<D, T, true><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg);
-  else
-    v_amax_kernel<D, T, false><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg);
-  return check_launch("v_amax");
+  for (int bh0 = 0; bh0 < bh; bh0 += kMaxGridY) {
+    dim3 grid(chunks, min(kMaxGridY, bh - bh0));
+    if (sg.cu != nullptr)
+      v_amax_kernel<D, T, true><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg, bh0);
+    else
+      v_amax_kernel<D, T, false><<<grid, 256, 0, stream>>>(vp, S, H, st, rows_per_cta, vs, sg, bh0);
+    if (check_launch("v_amax") != kStatusOk) return kStatusLaunch;
+  }
+  return kStatusOk;
 }
 
 // ------------------------------------------------------------------------------------------------

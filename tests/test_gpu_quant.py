@@ -92,3 +92,16 @@ def test_quant_large_head_count_property():
     vs = qt["vs"]
     ref = torch.linalg.vector_norm(v.float(), ord=float("inf"), dim=1)
     assert torch.equal(vs, ref)
+
+
+def test_more_planes_than_one_launch_holds():
+    """B * H above the grid's y limit (65535) is processed in several launches; the planes on both sides
+    of the split equal a separate call on just those heads."""
+    H, S, D = 70000, 40, 64
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q, k, v = (torch.randn(1, S, H, D, device="cuda", generator=g).bfloat16() for _ in range(3))
+    full = gpu_quant(q, k, v, "NHD")
+    sel = slice(65530, 65540)
+    part = gpu_quant(q[:, :, sel].contiguous(), k[:, :, sel].contiguous(), v[:, :, sel].contiguous(), "NHD")
+    for name in ("q8", "qs", "k8", "ks", "v8t", "vs"):
+        assert torch.equal(full[name][:, sel], part[name]), name

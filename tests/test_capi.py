@@ -60,3 +60,39 @@ def test_argument_errors_without_gpu():
     assert rc == _lib.SAGE_ERR_INVALID          # misaligned input pointer
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(rc, "sage_quant_q")
+
+
+def test_host_pipeline_planner_without_gpu():
+    """sage_attention_host's chunking and workspace are host arithmetic (148 SMs assumed without a GPU)."""
+    L = _lib.lib()
+    B, H, Hkv, S, D = 1, 40, 40, 32760, 128
+    hg = L.sage_host_heads_per_chunk(B, H, Hkv, S, S, D, 0)
+    assert 1 <= hg <= H
+    assert L.sage_host_heads_per_chunk(B, H, Hkv, S, S, D, 8) == 8
+    assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 0) % 4 == 0      # whole GQA groups
+    assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 6) == 0          # not a multiple of 4
+    assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 64) == 32        # clamped to H
+    a256 = lambda n: (n + 255) // 256 * 256
+    slot = 2 * a256(B * S * 8 * D * 2) + 2 * a256(B * S * 8 * D * 2) + a256(B * 8 * S * 4)
+    assert L.sage_host_workspace_bytes(B, H, Hkv, S, S, D, 8) == 2 * slot + a256(
+        L.sage_workspace_bytes(B, 8, 8, S, S, D))
+    rc = L.sage_attention_host(None, None, None, 0, B, H, Hkv, S, S, D, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0, None, 0, 0,
+                               0, None, 0, None, 0, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"non-null" in L.sage_last_error()
+
+
+def test_varlen_workspace_and_argument_checks_without_gpu():
+    L = _lib.lib()
+    nseq, H, Hkv, tq, tk, D = 8, 16, 16, 96635, 96635, 64
+    a256 = lambda n: (n + 255) // 256 * 256
+    pad = (tk + 31 * nseq + 31) // 32 * 32
+    parts = [H * tq * 64, H * tq * 4, Hkv * pad * 64, Hkv * pad // 32 * 4, Hkv * D * pad, nseq * Hkv * D * 4,
+             (nseq + 1) * 4, 4]
+    assert L.sage_varlen_workspace_bytes(nseq, H, Hkv, tq, tk, D) == sum(a256(p) for p in parts)
+    assert L.sage_varlen_workspace_bytes(nseq, H, Hkv, tq, tk, 80) == 0
+    rc = L.sage_attention_varlen(16, 16, 16, 0, nseq, H, 5, D, None, None, 100, 100, tq, tk, 8, 8, 8, 8, 8, 8, 0.0, 0,
+                                 16, 8, 8, None, None, 0, None, None)
+    assert rc == _lib.SAGE_ERR_UNSUPPORTED                  # 16 heads over 5 kv heads
+    rc = L.sage_attention_varlen(16, 16, 16, 0, nseq, H, Hkv, D, None, None, 100, 100, tq, tk, 8, 8, 8, 8, 8, 8, 0.0,
+                                 0, 16, 8, 8, None, None, 0, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"cu_seqlens" in L.sage_last_error()

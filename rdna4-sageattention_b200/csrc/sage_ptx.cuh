@@ -229,15 +229,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -255,11 +246,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// Barrier among `nthreads` threads (a multiple of 32) of the CTA on hardware barrier `id` (1..15).
-__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Per-warpgroup register budget (all four warps of a warpgroup execute it).
@@ -310,39 +296,10 @@ __device__ __forceinline__ int max32_tree(const uint32_t* v) {
   return max(__vimax3_s32(b0, b1, b2), b3);
 }
 
-// 2^y for both lanes of a packed pair on the FMA pipe (no MUFU): y = j + f with j = round(y) and
-// f in [-1/2, 1/2]; 2^f from a degree-5 polynomial fitted here for minimum relative error on that
-// interval (max relative error 2.3e-7 in fp32 Horner form, the same order as ex2.approx), and 2^j
-// added to the exponent field.  y is clamped to >= -126 so the exponent stays in range (2^-126 and
-// below do not change any sum the kernel forms).
-__device__ __forceinline__ void exp2_poly_x2(uint64_t y2, float& r0, float& r1) {
-  float y0, y1;
-  f2_unpack(y2, y0, y1);
-  y2 = f2_pack(fmaxf(y0, -126.0f), fmaxf(y1, -126.0f));
-  const uint64_t rnd = f2_pack(12582912.0f, 12582912.0f);     // 1.5 * 2^23: rounds to an integer
-  const uint64_t nrnd = f2_pack(-12582912.0f, -12582912.0f);
-  const uint64_t t = f2_add(y2, rnd);                           // bits: 0x4B400000 + round(y)
-  const uint64_t r = f2_add(t, nrnd);                           // round(y)
-  const uint64_t f = f2_fma(r, f2_pack(-1.0f, -1.0f), y2);      // y - round(y), exact
-  uint64_t p = f2_pack(1.3276470126584172e-03f, 1.3276470126584172e-03f);
-  p = f2_fma(p, f, f2_pack(9.675541892647743e-03f, 9.675541892647743e-03f));
-  p = f2_fma(p, f, f2_pack(5.550713464617729e-02f, 5.550713464617729e-02f));
-  p = f2_fma(p, f, f2_pack(2.4022120237350464e-01f, 2.4022120237350464e-01f));
-  p = f2_fma(p, f, f2_pack(6.931469440460205e-01f, 6.931469440460205e-01f));
-  p = f2_fma(p, f, f2_pack(1.0000001192092896f, 1.0000001192092896f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  // (bits of t) << 23 == round(y) << 23 modulo 2^32 (the low 9 bits of 0x4B400000 are zero)
-  r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 // int32 -> float32 for |s| < 2^22 with one integer add: the bit pattern of 1.5*2^23 + s is the float
-// 1.5*2^23 + s exactly (a float in [2^23, 2^24) has unit spacing), so float(s) = that - 1.5*2^23 and the
-// subtraction can be folded into a following fma.
+// 1.5*2^23 + s exactly (a float in [2^23, 2^24) has unit spacing), so float(s) = that - 1.5*2^23, and that
+// subtraction is exact too (the attention kernel does it on packed pairs).
 constexpr float kMagicF = 12582912.0f;   // 1.5 * 2^23
 constexpr int32_t kMagicI = 0x4B400000;  // bit pattern of 1.5 * 2^23
-__device__ __forceinline__ float magic_i2f_biased(int32_t s) { return __int_as_float(s + kMagicI); }
 
 }  // namespace sage

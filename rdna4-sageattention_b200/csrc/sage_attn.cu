@@ -2,7 +2,7 @@
 // reference's FlyDSL attention kernel (kernel_build/make_sage.py, make_sage_r2.py:54-269,
 // make_sage_pkg.py).
 //
-// One CTA owns QT query tiles of 128 rows of one (batch, head) and walks the keys in tiles of 128:
+// One CTA owns QT query tiles of 128 rows of one (batch, head) and walks the keys in tiles of BN:
 //   warp 4*QT      TMA producer: Q tiles once, then K (int8) and V^T (e4m3) tiles into an NST-deep ring
 //   warp 4*QT+1    MMA issuer (one thread): S_t = Q_t K^T with tcgen05.mma kind::i8 into TMEM (int32),
 //                  O_t += P_t V with kind::f8f6f4, P_t read from TMEM
@@ -10,9 +10,12 @@
 //                  TMEM, applies the per-32-key K scales, keeps the running max lazily (threshold 8 in
 //                  log2 units, as the reference), writes P_t = e4m3(exp2(...)) back into the S_t columns,
 //                  rescales O_t in TMEM when its max moved, and runs the epilogue
-// TMEM (512 columns): S/P slot 0 at column 0, slot 1 at column 128, O_t at 256 + t*D.
-// With QT = 2 (D <= 128) slot t belongs to Q tile t; with QT = 1 (D = 256) the two slots alternate
-// between consecutive key tiles so QK^T of tile j+1 overlaps the softmax of tile j.
+// TMEM (512 columns): S/P slots of BN columns from column 0, O_t at 256 + t*D.
+//   D = 64:      QT = 4, BN = 64 (four 128-row tiles, 16 softmax warps: 4 per SM sub-partition)
+//   D = 96, 128: QT = 2, BN = 128
+//   D = 256:     QT = 1, BN = 128; the two slots alternate between consecutive key tiles so QK^T of
+//                tile j+1 overlaps the softmax of tile j
+// With QT >= 2, slot t belongs to Q tile t.
 //
 // Arithmetic per query row i and key tile (matches the reference up to the tile width):
 //   c      = fp32(sm_scale*log2e) * qs_i
@@ -57,15 +60,18 @@ struct AttnParams {
 
 template <int D>
 struct AttnCfg {
-  static constexpr int QT = D <= 128 ? 2 : 1;                         // 128-row Q tiles per CTA
+  static constexpr int QT = D == 64 ? 4 : (D <= 128 ? 2 : 1);         // 128-row Q tiles per CTA
   static constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);    // int8 bytes per Q/K row
   static constexpr int SW = DK >= 128 ? 128 : 64;                     // swizzle width of a Q/K box
   static constexpr int BM = 128;
-  static constexpr int BN = 128;
+  static constexpr int BN = D == 64 ? 64 : 128;                       // keys per tile
+  static constexpr int NB = BN / 32;                                  // 32-key scale blocks per tile
+  static constexpr int SLOT = BN;                                     // TMEM columns of one S slot
+  static constexpr int VSW = BN;                                      // swizzle width of a V^T box row
   static constexpr int Q_TILE = BM * DK;
   static constexpr int K_TILE = BN * DK;
   static constexpr int V_TILE = D * BN;
-  static constexpr int NST = D == 64 ? 6 : (D == 256 ? 2 : 4);
+  static constexpr int NST = D == 64 ? 12 : (D == 256 ? 2 : 4);
 #ifndef SAGE_NO_SETMAXNREG
   // QT = 2: three full warpgroups (softmax 0, softmax 1, producer + MMA + two idle warps) so the
   // register file can be rebalanced towards the softmax warpgroups with setmaxnreg.
@@ -73,7 +79,7 @@ struct AttnCfg {
 #else
   static constexpr bool REBALANCE = false;
 #endif
-  static constexpr int THREADS = REBALANCE ? 384 : 128 * QT + 64;
+  static constexpr int THREADS = REBALANCE ? 384 : 128 * QT + 64;  // D = 64: 16 softmax warps + 2
   static constexpr int PRODUCER_WARP = 4 * QT;
   static constexpr int MMA_WARP = 4 * QT + 1;
   // registers per thread at launch (the launch bound gives 65536 / 384 rounded down to 8) and after
@@ -85,11 +91,20 @@ struct AttnCfg {
                 "setmaxnreg shares must sum to the launch allocation");
   static constexpr int O_COL = 256;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int NUM_BARS = 1 + 3 * NST + 2 + 2 + 2 + 1;
+  static constexpr int NUM_BARS = 1 + 3 * NST + 4 + 4 + 4 + 1;
   static constexpr int SMEM_BYTES = 1024 + QT * Q_TILE + NST * (K_TILE + V_TILE) + NUM_BARS * 8 + 16;
   // Keep a second CTA off the SM: its tcgen05.alloc of all 512 columns would have to wait.
   static constexpr int SMEM_ALLOC = SMEM_BYTES > 120 * 1024 ? SMEM_BYTES : 120 * 1024;
 };
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 
 __device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) {
   return (uint32_t)pack_e4m3x2(a, b) | ((uint32_t)pack_e4m3x2(c, d) << 16);
@@ -99,12 +114,12 @@ __device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) 
 // p = exp2(s * c * ks_b - c * m_new) for all 128 keys, packed to e4m3 (4 keys per word, key 4w+b in
 // byte b) and summed in fp32.  MASK: keys >= lim are excluded (edge tiles only).  Returns the sum of p
 // and the new running max in m_new (the caller derives the correction factor).
-template <bool MASK>
-__device__ __forceinline__ float softmax_tile(uint32_t (&s)[4][32], const float (&ksv)[4], float c, float m,
-                                              int kv0, int lim, float& m_new, uint32_t (&pw)[32]) {
+template <bool MASK, int NB>
+__device__ __forceinline__ float softmax_tile(uint32_t (&s)[NB][32], const float (&ksv)[NB], float c, float m,
+                                              int kv0, int lim, float& m_new, uint32_t (&pw)[NB * 8]) {
   if (MASK) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < NB; ++i)
 #pragma unroll
       for (int e = 0; e < 32; ++e)
         if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
@@ -112,7 +127,7 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&s)[4][32], const float 
   // lazy running max, decided per 32-key block in key order as the reference's 32-key tiles do
   m_new = m;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < NB; ++i) {
     const int mx = max32_tree(s[i]);
     if (!MASK || mx != INT32_MIN) {
       const float cand = fmaxf(m_new, (float)mx * ksv[i]);
@@ -124,7 +139,7 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&s)[4][32], const float 
   const uint64_t unbias2 = f2_pack(-kMagicF, -kMagicF);
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < NB; ++i) {
     const float cts = c * ksv[i];
     const uint64_t cts2 = f2_pack(cts, cts);
 #pragma unroll
@@ -177,9 +192,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   uint64_t* v_full = k_full + NST;
   uint64_t* kv_empty = v_full + NST;
   uint64_t* s_full = kv_empty + NST;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 2;
-  uint64_t* mma_drain = o_done + 2;
+  uint64_t* p_full = s_full + 4;
+  uint64_t* o_done = p_full + 4;
+  uint64_t* mma_drain = o_done + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* cta_abort = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -229,7 +244,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
@@ -292,7 +307,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
-      constexpr uint32_t kIdescQK = idesc_i8(128, 128);
+      constexpr uint32_t kIdescQK = idesc_i8(128, C::BN);
       constexpr uint32_t kIdescPV = idesc_e4m3(128, D);
       auto issue_s = [&](int j, int t, int slot) {
         const int st = j % NST;
@@ -302,24 +317,24 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
           const int kk = ks % (C::SW / 32);
           const uint64_t ad = smem_desc_kmajor(smem_u32(sQ + t * C::Q_TILE + a * C::BM * C::SW) + kk * 32, C::SW);
           const uint64_t bd = smem_desc_kmajor(smem_u32(sK + st * C::K_TILE + a * C::BN * C::SW) + kk * 32, C::SW);
-          mma_i8_ss(tmem + slot * 128, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
+          mma_i8_ss(tmem + slot * C::SLOT, ad, bd, kIdescQK, ks > 0 ? 1u : 0u);
         }
         tc_commit(&s_full[slot]);
       };
       auto issue_pv = [&](int j, int t, int slot) {
         const int st = j % NST;
 #pragma unroll
-        for (int ks = 0; ks < C::BN / 32; ++ks) {
-          const uint64_t bd = smem_desc_kmajor(smem_u32(sV + st * C::V_TILE) + ks * 32, 128);
-          mma_f8_ts(tmem + C::O_COL + t * D, tmem + slot * 128 + ks * 8, bd, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 0; ks < C::NB; ++ks) {
+          const uint64_t bd = smem_desc_kmajor(smem_u32(sV + st * C::V_TILE) + ks * 32, C::VSW);
+          mma_f8_ts(tmem + C::O_COL + t * D, tmem + slot * C::SLOT + ks * 8, bd, kIdescPV,
+                    (j > 0 || ks > 0) ? 1u : 0u);
         }
         tc_commit(&o_done[t]);
       };
       bool ok = mbar_wait(q_full, 0, wc) && mbar_wait(&k_full[0], 0, wc);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0, 0);
-        if (QT == 2) issue_s(0, 1, 1);
+        for (int t = 0; t < QT; ++t) issue_s(0, t, t);
       }
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % NST;
@@ -327,20 +342,23 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         const bool more = j + 1 < n_tiles;
         const int st1 = (j + 1) % NST;
         const uint32_t ph1 = ((j + 1) / NST) & 1;
-        if (QT == 2) {
-          // V(j) and K(j+1) land long before P_0(j): wait for them first, so that nothing but the P wait
-          // sits between the softmax announcing P and the tensor core receiving PV and the next QK^T
+        if (QT >= 2) {
+          // V(j) and K(j+1) land long before P_0(j): wait for them first, so that nothing but the P waits
+          // sit between the softmax announcing P and the tensor core receiving PV and the next QK^T
           if (!mbar_wait(&v_full[st], ph, wc)) break;
           if (more && !mbar_wait(&k_full[st1], ph1, wc)) break;
-          if (!mbar_wait(&p_full[0], j & 1, wc)) break;
-          tc_fence_after();
-          issue_pv(j, 0, 0);
-          if (more) issue_s(j + 1, 0, 0);
-          if (!mbar_wait(&p_full[1], j & 1, wc)) break;
-          tc_fence_after();
-          issue_pv(j, 1, 1);
-          tc_commit(&kv_empty[st]);
-          if (more) issue_s(j + 1, 1, 1);
+          bool tiles_ok = true;
+          for (int t = 0; t < QT; ++t) {
+            if (!mbar_wait(&p_full[t], j & 1, wc)) {
+              tiles_ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(j, t, t);
+            if (t == QT - 1) tc_commit(&kv_empty[st]);
+            if (more) issue_s(j + 1, t, t);
+          }
+          if (!tiles_ok) break;
         } else {
           if (more) {
             if (!mbar_wait(&k_full[st1], ph1, wc)) break;
@@ -373,18 +391,19 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    float ksn[4];  // K scales of the next tile, loaded one iteration ahead
+    constexpr int NB = C::NB;
+    float ksn[NB];  // K scales of the next tile, loaded one iteration ahead
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ksn[i] = i < nkb ? __ldg(ksb + i) : 0.f;
+    for (int i = 0; i < NB; ++i) ksn[i] = i < nkb ? __ldg(ksb + i) : 0.f;
     for (int j = 0; j < n_tiles; ++j) {
-      const int slot = QT == 2 ? t : (j & 1);
-      const uint32_t sph = QT == 2 ? (j & 1) : ((j >> 1) & 1);
+      const int slot = QT >= 2 ? t : (j & 1);
+      const uint32_t sph = QT >= 2 ? (j & 1) : ((j >> 1) & 1);
       const int kv0 = j * C::BN;
-      float ksv[4];
+      float ksv[NB];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < NB; ++i) {
         ksv[i] = ksn[i];
-        const int kb = (j + 1) * 4 + i;
+        const int kb = (j + 1) * NB + i;
         ksn[i] = kb < nkb ? __ldg(ksb + kb) : 0.f;
       }
       if (!mbar_wait(&s_full[slot], sph, wc)) {
@@ -392,23 +411,26 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t s[4][32];
+      uint32_t s[NB][32];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tmem_ld32(tl + slot * 128 + i * 32, s[i]);
+      for (int i = 0; i < NB; ++i) tmem_ld32(tl + slot * C::SLOT + i * 32, s[i]);
       tmem_wait_ld();
       const bool need_mask = (kv0 + C::BN > Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
       const int lim = min(Skv, CAUSAL ? last_key + 1 : Skv);  // keys < lim are kept
-      uint32_t pw[32];
+      uint32_t pw[NB * 8];
       float sum;
       float m_new;
       if (need_mask)
-        sum = softmax_tile<true>(s, ksv, c, m, kv0, lim, m_new, pw);
+        sum = softmax_tile<true, NB>(s, ksv, c, m, kv0, lim, m_new, pw);
       else
-        sum = softmax_tile<false>(s, ksv, c, m, kv0, lim, m_new, pw);
+        sum = softmax_tile<false, NB>(s, ksv, c, m, kv0, lim, m_new, pw);
       const bool need = m_new != m;
       const float corr = need ? fast_exp2((m - m_new) * c) : 1.0f;
       l = corr * l + sum;
-      tmem_st32(tl + slot * 128, pw);
+      if constexpr (NB == 4)
+        tmem_st32(tl + slot * C::SLOT, pw);
+      else
+        tmem_st16(tl + slot * C::SLOT, pw);
       if (__any_sync(0xffffffffu, need && j > 0)) {
         // the previous P.V of this tile must have landed before O is rescaled
         if (!mbar_wait(&o_done[t], (j - 1) & 1, wc)) {
@@ -429,7 +451,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[slot]);
+      if (lane == 0) mbar_arrive(&p_full[QT >= 2 ? t : slot]);
       m = m_new;
     }
     // ---------------------------------------------------------------- epilogue
@@ -539,8 +561,9 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
   const CUtensorMapSwizzle qk_sw = C::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   if (!make_map(&mq, a.q8, C::DK, q_rows, q_planes, C::DK, (uint64_t)q_rows * C::DK, C::SW, 128, qk_sw) ||
-      !make_map(&mk, a.k8, C::DK, k_rows, k_planes, C::DK, (uint64_t)k_rows * C::DK, C::SW, 128, qk_sw) ||
-      !make_map(&mv, a.v8t, k_rows, D, k_planes, k_rows, (uint64_t)k_rows * D, 128, D, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_map(&mk, a.k8, C::DK, k_rows, k_planes, C::DK, (uint64_t)k_rows * C::DK, C::SW, C::BN, qk_sw) ||
+      !make_map(&mv, a.v8t, k_rows, D, k_planes, k_rows, (uint64_t)k_rows * D, C::BN, D,
+                C::VSW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
     return kStatusInvalid;
   AttnParams p;
   p.qs = a.qs;

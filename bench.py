@@ -274,7 +274,7 @@ def run_hunyuan_cp(args):
         print(json.dumps({"metric": "ms/call & TOPS, 67576-tok 24-head d128 sageattn (context parallel)",
                           "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
                           "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                          "scaling": "strong", "vs_baseline": None, "dtype": "int8 QK / e4m3 PV (bf16 in, bf16 out)",
+                          "scaling": "strong", "vs_baseline": None, "dtype": "int8/e4m3",
                           "data": "synthetic",
                           "config": {"workload": "hunyuanvideo-544p self-attention call, sequence split over ranks",
                                      "global_batch": 1, "seq_len": n, "parallelism": f"cp{world}"}}), flush=True)
@@ -419,10 +419,12 @@ def run_ours(args):
             "vs_baseline": value / (ops_per_call() / (REF_WAN_MS * 1e-3) / 1e12),
             "vs_baseline_basis": "value / 139.1 TOPS (reference README.md:194: 158 ms/call for this shape on "
                                  "RX 9070 XT)",
-            "dtype": "int8 QK / e4m3 PV (bf16 in, bf16 out)", "data": "synthetic",
+            "dtype": "int8/e4m3", "data": "synthetic",
             "config": {"workload": "wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16, "
                                    "K + per-channel offset N(0, std 2))",
-                       "model": "wan2.1-14b-480p", "global_batch": 1 if args.strong else world, "seq_len": N,
+                       "arithmetic": "int8 QK^T (int32 accumulate), fp32 softmax, e4m3 PV (fp32 accumulate); "
+                                     "bf16 in and out",
+                       "global_batch": 1 if args.strong else world, "seq_len": N,
                        "heads_per_rank": heads,
                        "parallelism": (f"heads split over {world} ranks" if args.strong else
                                        f"dp{world}: one call's (batch, head) units per rank, no collective"),

@@ -40,6 +40,8 @@ import torch  # noqa: E402
 B, H, N, D = 1, 40, 32760, 128
 REF_WAN_MS = 158.0          # reference README.md:194, Wan 2.1 14B 480p, RX 9070 XT, ms per call
 METRIC = "ms/call & TOPS per GPU, 32760-tok 40-head d128 sageattn; % int8/fp8 TC peak"
+WORKLOAD = ("wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16, "
+            "K + per-channel offset N(0, std 2))")
 
 
 def ops_per_call(b=B, h=H, n=N, d=D):
@@ -173,8 +175,7 @@ def run_reference(args):
     line = {"metric": METRIC, "value": value, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 * H / heads,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16)",
-                       "global_batch": 1, "seq_len": N, "parallelism": "host cores"},
+            "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": N, "parallelism": "host cores"},
             "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": f"{heads} of {H} heads per step through the reference's SDPA fallback on "
                                        f"CPU (torch bf16 SDPA), ms_per_step scaled to the full 40-head call"},
@@ -420,8 +421,7 @@ def run_ours(args):
             "vs_baseline_basis": "value / 139.1 TOPS (reference README.md:194: 158 ms/call for this shape on "
                                  "RX 9070 XT)",
             "dtype": "int8/e4m3", "data": "synthetic",
-            "config": {"workload": "wan2.1-14b-480p self-attention call (B=1 H=40 N=32760 D=128 NHD bf16, "
-                                   "K + per-channel offset N(0, std 2))",
+            "config": {"workload": WORKLOAD,
                        "arithmetic": "int8 QK^T (int32 accumulate), fp32 softmax, e4m3 PV (fp32 accumulate); "
                                      "bf16 in and out",
                        "global_batch": 1 if args.strong else world, "seq_len": N,

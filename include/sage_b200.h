@@ -70,6 +70,18 @@ int sage_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, 
                   int64_t skh, int64_t svb, int64_t svs, int64_t svh, const float* vs, int8_t* k8, float* ks,
                   uint8_t* v8t, void* stream);
 
+/* The three quantiser passes above and the sm_scale fold (_attention.py:121-131) in ONE launch, for dense
+ * calls: V channel amax, q8/qs (qs multiplied by `fold`), k8/ks and v8t, with the outputs of
+ * sage_v_amax + sage_quant_q + sage_quant_kv bit for bit.  Q is (B, Sq, H, D), K and V (B, Skv, Hkv, D),
+ * strides as above.  vs [B, Hkv, D] receives the channel amax; `sync` is device scratch of
+ * sage_quant_sync_ints(B, Hkv) ints; the call zeroes both (one memset when sync directly follows vs).
+ * `status` (nullable = the library's own word) receives SAGE_ERR_TIMEOUT if an internal wait expires. */
+int sage_quant_sync_ints(int B, int Hkv);
+int sage_quant_qkv(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                   int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                   int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
+                   float* vs, int* sync, int* status, void* stream);
+
 /* Replaces the attention launch (_attention.py:133-139; kernel make_sage_r2.py:54-269): out[b, s, h, :]
  * (element strides osb, oss, osh) in out_dtype; optional lse [B, H, Sq] (natural log of the softmax
  * denominator of the dequantised logits); causal is bottom-right aligned.  `status` (nullable) is a
@@ -82,7 +94,9 @@ int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const flo
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D);
 
 /* The whole hot path of rdna4_sage._attention.attention (_attention.py:97-140) in one call:
- * V amax, quantise Q, quantise K+V, attention.  sm_scale <= 0 selects 1/sqrt(D); any other value
+ * quantisers, then attention.  The quantisers run as one sage_quant_qkv launch when Skv <= 8192 and
+ * D <= 128 (where it is the faster choice) and as sage_v_amax + sage_quant_q + sage_quant_kv otherwise;
+ * the outputs are identical either way.  sm_scale <= 0 selects 1/sqrt(D); any other value
  * not within 1e-6 relative of 1/sqrt(D) is folded into the Q scales as the reference does. */
 int sage_attention(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
                    int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,

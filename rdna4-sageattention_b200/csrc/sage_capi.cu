@@ -73,6 +73,7 @@ struct Workspace {
   float* ks;
   uint8_t* v8t;
   float* vs;
+  int* sync;  // work counters of the single-launch quantiser, directly after vs (one memset for both)
   size_t bytes;
 };
 
@@ -92,7 +93,8 @@ static Workspace carve(void* base, int B, int H, int Hkv, int Sq, int Skv, int D
   w.k8 = reinterpret_cast<int8_t*>(take((size_t)B * Hkv * sp * dk));
   w.ks = reinterpret_cast<float*>(take((size_t)B * Hkv * (sp / kKvBlock) * 4));
   w.v8t = reinterpret_cast<uint8_t*>(take((size_t)B * Hkv * D * sp));
-  w.vs = reinterpret_cast<float*>(take((size_t)B * Hkv * D * 4));
+  w.vs = reinterpret_cast<float*>(take(((size_t)B * Hkv * D + (size_t)quant_fused_sync_ints(B, Hkv)) * 4));
+  w.sync = w.vs ? reinterpret_cast<int*>(w.vs + (size_t)B * Hkv * D) : nullptr;
   w.bytes = off;
   return w;
 }
@@ -135,6 +137,14 @@ static VarlenWorkspace carve_varlen(void* base, int nseq, int H, int Hkv, int to
   w.bytes = off;
   return w;
 }
+
+// Quantiser choice of sage_attention (outputs are identical either way).  Measured on B200 with bf16
+// inputs (CUDA events, L2 flushed): the single launch is faster while a (batch, kv head) plane is short
+// (B1 H24 S4608 D128: 0.060 vs 0.071 ms; B4 H32/8 S8192: 0.202 vs 0.214 ms; B1 H40 S8192: 0.144 vs
+// 0.159 ms) and slower for long planes and for D = 256, whose two shared-memory stages leave one CTA per
+// SM (B1 H40 S32760: 0.601 vs 0.542 ms; B1 H24 S67576: 0.918 vs 0.663 ms; B2 H16 S8192 D256: 0.470 vs
+// 0.273 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
+static bool use_fused_quantiser(int Skv, int D) { return Skv <= 8192 && D <= 128; }
 
 // math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)
 static bool isclose_rel(double a, double b, double rel) {
@@ -193,6 +203,38 @@ int sage_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, 
                          static_cast<cudaStream_t>(stream));
 }
 
+int sage_quant_sync_ints(int B, int Hkv) { return (B > 0 && Hkv > 0) ? quant_fused_sync_ints(B, Hkv) : 0; }
+
+int sage_quant_qkv(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                   int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                   int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
+                   float* vs, int* sync, int* status, void* stream) {
+  g_error[0] = 0;
+  int rc = check_common(dtype, B, Sq, H, D);
+  if (rc != SAGE_OK) return rc;
+  if (Hkv <= 0 || H % Hkv != 0 || Skv <= 0) {
+    set_error("heads %d must be a multiple of kv heads %d and kv length %d positive", H, Hkv, Skv);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  rc = check_input(q, qsb, qss, qsh, "q");
+  if (rc == SAGE_OK) rc = check_input(k, ksb, kss, ksh, "k");
+  if (rc == SAGE_OK) rc = check_input(v, vsb, vss, vsh, "v");
+  if (rc != SAGE_OK) return rc;
+  if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8t) || qs == nullptr || ks == nullptr || vs == nullptr ||
+      sync == nullptr) {
+    set_error("q8 / k8 / v8t must be 16-byte aligned, qs, ks, vs and sync non-null");
+    return SAGE_ERR_INVALID;
+  }
+  int* word = status != nullptr ? status : default_status_word();
+  if (word == nullptr) {
+    set_error("no status word on this device");
+    return SAGE_ERR_LAUNCH;
+  }
+  return launch_quant_fused(q, k, v, dtype, B, H, Hkv, Sq, Skv, D, Strides3{qsb, qss, qsh}, Strides3{ksb, kss, ksh},
+                            Strides3{vsb, vss, vsh}, fold, q8, qs, k8, ks, v8t, vs, sync, word,
+                            static_cast<cudaStream_t>(stream));
+}
+
 int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
                   const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D, int causal,
                   int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream) {
@@ -239,10 +281,16 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
   if (sm_scale > 0.0 && !isclose_rel(sm_scale, 1.0 / std::sqrt((double)D), 1e-6))
     fold = (float)(sm_scale * std::sqrt((double)D));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = sage_v_amax(v, dtype, B, Skv, Hkv, D, vsb, vss, vsh, w.vs, s);
-  if (rc == SAGE_OK) rc = sage_quant_q(q, dtype, B, Sq, H, D, qsb, qss, qsh, fold, w.q8, w.qs, s);
-  if (rc == SAGE_OK)
-    rc = sage_quant_kv(k, v, dtype, B, Skv, Hkv, D, ksb, kss, ksh, vsb, vss, vsh, w.vs, w.k8, w.ks, w.v8t, s);
+  int rc;
+  if (use_fused_quantiser(Skv, D)) {
+    rc = sage_quant_qkv(q, k, v, dtype, B, H, Hkv, Sq, Skv, D, qsb, qss, qsh, ksb, kss, ksh, vsb, vss, vsh, fold,
+                        w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, w.sync, status, s);
+  } else {
+    rc = sage_v_amax(v, dtype, B, Skv, Hkv, D, vsb, vss, vsh, w.vs, s);
+    if (rc == SAGE_OK) rc = sage_quant_q(q, dtype, B, Sq, H, D, qsb, qss, qsh, fold, w.q8, w.qs, s);
+    if (rc == SAGE_OK)
+      rc = sage_quant_kv(k, v, dtype, B, Skv, Hkv, D, ksb, kss, ksh, vsb, vss, vsh, w.vs, w.k8, w.ks, w.v8t, s);
+  }
   if (rc == SAGE_OK)
     rc = sage_attn_fwd(w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, out, dtype, B, H, Hkv, Sq, Skv, D, causal, osb, oss, osh,
                        lse, status, s);

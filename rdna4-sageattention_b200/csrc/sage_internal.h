@@ -61,6 +61,14 @@ int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H
                     const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream,
                     const Segs& sg = Segs());
 
+// V amax, Q, K and V quantisation of a dense call in one launch (the single-launch quantiser).  `vs` is
+// [B, Hkv, D] and `sync` holds quant_fused_sync_ints(B, Hkv) ints; both are zeroed by the launcher
+// (with one memset when sync directly follows vs).  Outputs equal the separate launches' bit for bit.
+int quant_fused_sync_ints(int B, int Hkv);
+int launch_quant_fused(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                       int D, Strides3 sq, Strides3 sk, Strides3 sv, float fold, int8_t* q8, float* qs, int8_t* k8,
+                       float* ks, uint8_t* v8t, float* vs, int* sync, int* status, cudaStream_t stream);
+
 struct AttnArgs {
   const int8_t* q8;
   const float* qs;

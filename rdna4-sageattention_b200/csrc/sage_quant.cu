@@ -11,6 +11,8 @@
 // butterflies); it equals the reference's fp32-accumulated product with Hm up to fp32 summation order.
 // One thread per token row: the row's 2*D bytes are contiguous, so each thread streams them with 16-byte
 // loads (every L2 sector it touches is used in full) and writes its code row with 16-byte stores.
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -71,15 +73,25 @@ __device__ __forceinline__ void fwht(float* x) {
 constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)
 constexpr int kMaxGridY = 65535;  // (batch, head) planes per launch (the grid's y limit)
 
-// fp32 values of N consecutive channels of one token row read straight from global memory (16-byte
-// loads; the row's bytes are contiguous), rotated by the Walsh-Hadamard transform when `rot`.
-// Rows past the end of the sequence read as zeros.
-template <int N, typename T>
+// 16 bytes of a row: from global memory through the read-only path (zeros when !valid), or from a
+// shared-memory stage whose rows past the end of the sequence were zero-filled when they were copied.
+template <bool SMEM>
+__device__ __forceinline__ uint4 row_chunk(const uint4* p, bool valid) {
+  if constexpr (SMEM) {
+    return *p;
+  } else {
+    return valid ? __ldg(p) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// fp32 values of N consecutive channels of one token row (16-byte loads; the row's bytes are contiguous
+// in global memory and in a shared-memory stage alike), rotated by the Walsh-Hadamard transform when
+// `rot`.  Rows past the end of the sequence read as zeros.
+template <int N, typename T, bool SMEM = false>
 __device__ __forceinline__ void row_values(const T* __restrict__ row, bool valid, bool rot, float* x) {
   uint4 v[N / 8];
 #pragma unroll
-  for (int i = 0; i < N / 8; ++i)
-    v[i] = valid ? __ldg(reinterpret_cast<const uint4*>(row) + i) : make_uint4(0, 0, 0, 0);
+  for (int i = 0; i < N / 8; ++i) v[i] = row_chunk<SMEM>(reinterpret_cast<const uint4*>(row) + i, valid);
 #pragma unroll
   for (int i = 0; i < N / 8; ++i) {
     const T* e = reinterpret_cast<const T*>(&v[i]);
@@ -140,25 +152,25 @@ __device__ __forceinline__ void store_codes(const float* x, float scale, int8_t*
 // (amax_fn is a warp reduction, so every lane of the warp calls it).  D = 256 is two independent
 // 128-wide rotation blocks sharing one scale; the first block is reloaded and recomputed after the
 // scale is known so that only 128 values are live at a time.
-template <int D, typename T, typename AmaxFn>
+template <int D, typename T, bool SMEM = false, typename AmaxFn>
 __device__ __forceinline__ float quant_row(const T* __restrict__ row, bool valid, int8_t* out_row, bool store,
                                            AmaxFn amax_fn) {
   constexpr bool kRot = (D & (D - 1)) == 0;
   constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
   if constexpr (D == 256) {
     float x[128];
-    row_values<128, T>(row, valid, true, x);
+    row_values<128, T, SMEM>(row, valid, true, x);
     const float a0 = abs_max<128>(x);
-    row_values<128, T>(row + 128, valid, true, x);
+    row_values<128, T, SMEM>(row + 128, valid, true, x);
     const float a1 = abs_max<128>(x);
     const float scale = __fdiv_rn(fmaxf(amax_fn(fmaxf(a0, a1)), 1e-12f), 127.0f);
     if (store) store_codes<128>(x, scale, out_row + 128);
-    row_values<128, T>(row, valid, true, x);
+    row_values<128, T, SMEM>(row, valid, true, x);
     if (store) store_codes<128>(x, scale, out_row);
     return scale;
   } else {
     float x[DK];
-    row_values<D, T>(row, valid, kRot, x);
+    row_values<D, T, SMEM>(row, valid, kRot, x);
 #pragma unroll
     for (int i = D; i < DK; ++i) x[i] = 0.f;
     const float scale = __fdiv_rn(fmaxf(amax_fn(abs_max<D>(x)), 1e-12f), 127.0f);
@@ -168,8 +180,53 @@ __device__ __forceinline__ float quant_row(const T* __restrict__ row, bool valid
 }
 
 // ------------------------------------------------------------------------------------------------
+// K + V row bodies, shared by the separate K+V kernel and the single-launch quantiser
+// ------------------------------------------------------------------------------------------------
+// K row of a 32-key scale block (the warp): codes when `inpad`, the block scale by lane 0 into *ks_entry.
+// Every lane of the warp calls this (the block amax is a warp reduction).
+template <int D, typename T, bool SMEM = false>
+__device__ __forceinline__ void quant_k_row(const T* __restrict__ krow, bool valid, bool inpad, int8_t* k8row,
+                                            float* ks_entry, int lane) {
+  const float kscale = quant_row<D, T, SMEM>(krow, valid, k8row, inpad, [](float a) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
+  });
+  if (lane == 0) *ks_entry = kscale;
+}
+
+// V row to e4m3 with the per-channel factors fac[c] = 448 / max(vs_c, 1e-30); channel c of this key goes
+// to vout[c * pitch] (the 32 lanes of a warp write 32 consecutive bytes of each channel row of v8t).
+template <int D, typename T, bool SMEM = false>
+__device__ __forceinline__ void quant_v_row(const T* __restrict__ vrow, bool valid, const float* fac, uint8_t* vout,
+                                            int64_t pitch) {
+#pragma unroll 2
+  for (int c = 0; c < D; c += 8) {
+    const uint4 raw = row_chunk<SMEM>(reinterpret_cast<const uint4*>(vrow + c), valid);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int kx = 0; kx < 8; kx += 2) {
+      const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
+      const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
+      const uint16_t pk = pack_e4m3x2(y0, y1);
+      vout[(int64_t)(c + kx) * pitch] = (uint8_t)(pk & 0xff);
+      vout[(int64_t)(c + kx + 1) * pitch] = (uint8_t)(pk >> 8);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Q: one thread per token row
 // ------------------------------------------------------------------------------------------------
+// Q row: codes and qs = scale / RB * fold (the sm_scale fold, _attention.py:130-131) when `valid`.
+template <int D, typename T, bool SMEM = false>
+__device__ __forceinline__ void quant_q_row(const T* __restrict__ row, bool valid, int8_t* q8row, float* qs_entry,
+                                            float fold) {
+  float scale = quant_row<D, T, SMEM>(row, valid, q8row, valid, [](float a) { return a; });
+  if (valid) {
+    if ((D & (D - 1)) == 0) scale = scale / (float)(D < 128 ? D : 128);
+    *qs_entry = scale * fold;
+  }
+}
+
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
                                                         float fold, int8_t* __restrict__ q8, float* __restrict__ qs,
@@ -181,11 +238,7 @@ __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x,
   const int s = blockIdx.x * kRows + threadIdx.x;
   const bool valid = s < S;
   const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h;
-  float scale = quant_row<D, T>(row, valid, q8 + ((int64_t)bh * S + s) * DK, valid, [](float a) { return a; });
-  if (valid) {
-    if ((D & (D - 1)) == 0) scale = scale / (float)(D < 128 ? D : 128);
-    qs[(int64_t)bh * S + s] = scale * fold;
-  }
+  quant_q_row<D, T>(row, valid, q8 + ((int64_t)bh * S + s) * DK, qs + (int64_t)bh * S + s, fold);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -229,30 +282,12 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
 
   // K: codes and the block scale (warp max of the 32 rows' amax)
   const T* krow = k + src_b * sk.b + (t0 + (valid ? s : 0)) * sk.s + (int64_t)h * sk.h;
-  const float kscale = quant_row<D, T>(krow, valid, k8 + orow * DK, inpad, [](float a) {
-    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
-  });
-  if (lane == 0) ks[orow / kKvBlock] = kscale;
+  quant_k_row<D, T>(krow, valid, inpad, k8 + orow * DK, ks + orow / kKvBlock, lane);
 
-  // V: per-channel scale to e4m3; channel c of this key goes to v8t[b, h, c, s] (32 lanes = 32
-  // consecutive bytes of each channel row)
+  // V: per-channel scale to e4m3
   if (!inpad) return;
   const T* vrow = v + src_b * sv.b + (t0 + (valid ? s : 0)) * sv.s + (int64_t)h * sv.h;
-  const int64_t spitch = pitch;
-  uint8_t* vout = v8t + vbase + s;
-#pragma unroll 2
-  for (int c = 0; c < D; c += 8) {
-    const uint4 raw = valid ? __ldg(reinterpret_cast<const uint4*>(vrow + c)) : make_uint4(0, 0, 0, 0);
-    const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-    for (int kx = 0; kx < 8; kx += 2) {
-      const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
-      const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
-      const uint16_t pk = pack_e4m3x2(y0, y1);
-      vout[(int64_t)(c + kx) * spitch] = (uint8_t)(pk & 0xff);
-      vout[(int64_t)(c + kx + 1) * spitch] = (uint8_t)(pk >> 8);
-    }
-  }
+  quant_v_row<D, T>(vrow, valid, fac, v8t + vbase + s, pitch);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -301,6 +336,244 @@ __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, in
     for (int k = 0; k < 8; ++k)
       atomicMax(reinterpret_cast<unsigned int*>(vs + (int64_t)bh * D + threadIdx.x * 8 + k), __float_as_uint(acc[k]));
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Single-launch quantiser (dense calls): V amax, Q, K and V in one persistent kernel
+// ------------------------------------------------------------------------------------------------
+// The V codes need the channel amax over the whole sequence of their (batch, kv head) plane, so one
+// launch holds a dependency: V of a plane is quantised only after every row of that plane has been
+// reduced.  The work is a list of 128-row items taken in order from a global counter:
+//   A items of wave w: V amax tiles and K tiles of the wave's kv planes, then the Q tiles of the query
+//                      heads that share those kv planes (no dependency);
+//   B items of wave w: V tiles to e4m3, after all of wave w's V amax items are counted done.
+// Waves are groups of P consecutive kv planes, and the list runs A(0), A(1) B(0), A(2) B(1), ...,
+// B(W-1): the V rows of wave w are read by its amax items and read again by its B items one wave
+// later, while they are still in L2 (P is chosen so that a wave's V bytes are a small part of L2).  An
+// item is taken only after every earlier item has been taken by a running CTA, and A items never wait,
+// so every wait ends without any assumption on how many CTAs are resident.  Waits are still bounded:
+// after kWaitLimitNs the kernel stores SAGE_ERR_TIMEOUT into the status word, raises the abort flag
+// sync[1] and skips the item (and every later CTA skips its waits).
+//
+// Each CTA copies the rows of its next item into a shared-memory stage (cp.async, 16 bytes per copy,
+// rows past the end of the sequence zero-filled) while it computes the current one from the other
+// stage, so the loads of one item overlap the arithmetic of the previous one.  A stage row is the
+// token row's 2*D bytes plus 16 bytes of padding: an odd number of 16-byte chunks per row, so the 32
+// threads of a warp (one row each) reading the same chunk of their rows hit distinct banks.
+enum : int { kItemVAmax = 0, kItemK = 1, kItemQ = 2, kItemV = 3 };
+
+struct FusedPlan {
+  int P;       // kv planes per wave (divides B * Hkv)
+  int W;       // waves
+  int Tk, Tq;  // 128-row tiles of a kv plane (over the padded length) / of a query plane
+  int g;       // query heads per kv head
+  int LA, LB;  // items in a wave's A part (P*Tk amax + P*Tk K + P*g*Tq Q) / B part (P*Tk V)
+  int lag;     // B items of wave w follow the A items of wave w + lag (1 <= lag <= W)
+  int total;   // all items
+};
+
+struct FusedItem {
+  int type, wave, plane, tile;  // plane: kv plane (b * Hkv + h) or, for Q, query plane (b * H + h)
+};
+
+__device__ __forceinline__ FusedItem decode_item(int cur, const FusedPlan& pl) {
+  // slots [0, lag) hold A items only, slots [lag, W) hold A(s) then B(s - lag), and slots [W, W + lag)
+  // hold B items only
+  int wave, off;
+  bool is_a;
+  const int head = pl.lag * pl.LA;
+  const int per = pl.LA + pl.LB;
+  if (cur < head) {
+    wave = cur / pl.LA, off = cur - wave * pl.LA, is_a = true;
+  } else if (cur < head + (pl.W - pl.lag) * per) {
+    const int j = cur - head;
+    const int sl = j / per;
+    off = j - sl * per;
+    is_a = off < pl.LA;
+    wave = is_a ? sl + pl.lag : sl;
+    if (!is_a) off -= pl.LA;
+  } else {
+    const int j = cur - head - (pl.W - pl.lag) * per;
+    wave = pl.W - pl.lag + j / pl.LB, off = j % pl.LB, is_a = false;
+  }
+  FusedItem it;
+  it.wave = wave;
+  const int pt = pl.P * pl.Tk;
+  if (!is_a) {
+    it.type = kItemV, it.plane = wave * pl.P + off / pl.Tk, it.tile = off % pl.Tk;
+  } else if (off < 2 * pt) {
+    const int o = off < pt ? off : off - pt;
+    it.type = off < pt ? kItemVAmax : kItemK, it.plane = wave * pl.P + o / pl.Tk, it.tile = o % pl.Tk;
+  } else {
+    const int o = off - 2 * pt;
+    it.type = kItemQ, it.plane = wave * pl.P * pl.g + o / pl.Tq, it.tile = o % pl.Tq;
+  }
+  return it;
+}
+
+// sync[0]: item counter; sync[1]: abort flag; sync[2 + w]: finished V amax items of wave w.  Zero on entry.
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool wait_wave(const int* ctr, int need, int* abort_flag, int* status) {
+  const uint64_t t0 = global_timer_ns();
+  while (ld_acquire(ctr) < need) {
+    if (ld_acquire(abort_flag) != 0) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      atomicCAS(status, 0, kStatusTimeout);
+      atomicExch(abort_flag, 1);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// 16-byte chunks per stage row (2*D bytes + 16 of padding) and bytes per stage
+template <int D>
+constexpr int stage_row_chunks() { return D / 8 + 1; }
+template <int D>
+constexpr int stage_bytes() { return kRows * stage_row_chunks<D>() * 16; }
+
+// Copy rows [r0, r0 + kRows) of one (batch, head) plane (plane_base = its row 0, ss the row stride)
+// into `stage`; rows at or past S are zero-filled (the copy reads no bytes for them).
+template <int D, typename T>
+__device__ __forceinline__ void stage_rows(uint4* stage, const T* plane_base, int64_t ss, int r0, int S) {
+  constexpr int C = D / 8;
+  constexpr int RS = stage_row_chunks<D>();
+  for (int idx = threadIdx.x; idx < kRows * C; idx += kRows) {
+    const int r = idx / C, c = idx - r * C;
+    const int s = r0 + r;
+    const bool ok = s < S;
+    cp_async16(stage + r * RS + c, plane_base + (int64_t)(ok ? s : 0) * ss + c * 8, ok ? 16 : 0);
+  }
+}
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kRows) quant_fused_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                            const T* __restrict__ v, int Sq, int Skv, int H, int Hkv,
+                                                            Strides3 sq, Strides3 sk, Strides3 sv, float fold,
+                                                            int8_t* __restrict__ q8, float* __restrict__ qs,
+                                                            int8_t* __restrict__ k8, float* __restrict__ ks,
+                                                            uint8_t* __restrict__ v8t, float* __restrict__ vs,
+                                                            int* __restrict__ sync, int* __restrict__ status,
+                                                            FusedPlan pl) {
+  constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+  constexpr int G = D / 8;             // 16-byte chunks of a row (V amax mapping: one chunk per thread)
+  constexpr int RSTEP = kRows / G;     // rows per pass of the V amax mapping
+  constexpr int RS = stage_row_chunks<D>();
+  extern __shared__ uint4 stages[];    // two stages of kRows padded rows
+  __shared__ int s_item[3];
+  __shared__ int s_go;
+  __shared__ float fac[D];
+  __shared__ float red[kRows][8];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int spad = (Skv + kKvBlock - 1) / kKvBlock * kKvBlock;
+
+  // issue the copies of item `it` into stage `st` (one commit group per item, empty past the end)
+  auto load_item = [&](int idx, int st) {
+    if (idx < pl.total) {
+      const FusedItem it = decode_item(idx, pl);
+      uint4* dst = stages + st * kRows * RS;
+      if (it.type == kItemQ) {
+        const int b = it.plane / H, h = it.plane - b * H;
+        stage_rows<D, T>(dst, q + (int64_t)b * sq.b + (int64_t)h * sq.h, sq.s, it.tile * kRows, Sq);
+      } else {
+        const int b = it.plane / Hkv, h = it.plane - b * Hkv;
+        if (it.type == kItemK)
+          stage_rows<D, T>(dst, k + (int64_t)b * sk.b + (int64_t)h * sk.h, sk.s, it.tile * kRows, Skv);
+        else
+          stage_rows<D, T>(dst, v + (int64_t)b * sv.b + (int64_t)h * sv.h, sv.s, it.tile * kRows, Skv);
+      }
+    }
+    cp_async_commit();
+  };
+
+  if (tid == 0) {
+    s_item[0] = atomicAdd(&sync[0], 1);
+    s_item[1] = atomicAdd(&sync[0], 1);
+  }
+  __syncthreads();
+  load_item(s_item[0], 0);
+  for (int n = 0;; ++n) {
+    const int cur = s_item[n % 3];
+    if (cur >= pl.total) break;
+    const int nxt = s_item[(n + 1) % 3];
+    if (tid == 0) s_item[(n + 2) % 3] = atomicAdd(&sync[0], 1);  // two items ahead
+    load_item(nxt, (n + 1) & 1);
+    cp_async_wait_prev();  // this thread's copies of the current item have landed
+    __syncthreads();       // ... and every other thread's
+    const FusedItem it = decode_item(cur, pl);
+    const uint4* stage = stages + (n & 1) * kRows * RS;
+    const T* my_row = reinterpret_cast<const T*>(stage + tid * RS);
+    const int s = it.tile * kRows + tid;
+    if (it.type == kItemVAmax) {
+      float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int gch = tid % G, rr0 = tid / G;
+      if (rr0 < RSTEP) {
+#pragma unroll 4
+        for (int r = rr0; r < kRows; r += RSTEP) {  // zero-filled rows past Skv leave the max unchanged
+          const uint4 raw = stage[r * RS + gch];
+          const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+          for (int kx = 0; kx < 8; ++kx) m[kx] = fmaxf(m[kx], fabsf(to_f32<T>(e[kx])));
+        }
+      }
+#pragma unroll
+      for (int kx = 0; kx < 8; ++kx) red[tid][kx] = m[kx];
+      __syncthreads();
+      if (tid < G) {
+        float acc[8];
+#pragma unroll
+        for (int kx = 0; kx < 8; ++kx) acc[kx] = red[tid][kx];
+        for (int rr = 1; rr < RSTEP; ++rr)
+#pragma unroll
+          for (int kx = 0; kx < 8; ++kx) acc[kx] = fmaxf(acc[kx], red[rr * G + tid][kx]);
+        // max via the order of non-negative float bit patterns (vs is zero on entry)
+#pragma unroll
+        for (int kx = 0; kx < 8; ++kx)
+          atomicMax(reinterpret_cast<unsigned int*>(vs + (int64_t)it.plane * D + tid * 8 + kx),
+                    __float_as_uint(acc[kx]));
+      }
+      // the CTA's amax updates are ordered before the arrival by the barrier and thread 0's fence
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        atomicAdd(&sync[2 + it.wave], 1);
+      }
+    } else if (it.type == kItemK) {
+      if (s - lane < spad) {  // the warp's scale block exists
+        const int64_t orow = (int64_t)it.plane * spad + s;
+        quant_k_row<D, T, true>(my_row, true, s < spad, k8 + orow * DK, ks + orow / kKvBlock, lane);
+      }
+    } else if (it.type == kItemQ) {
+      const bool valid = s < Sq;
+      quant_q_row<D, T, true>(my_row, valid, q8 + ((int64_t)it.plane * Sq + s) * DK, qs + (int64_t)it.plane * Sq + s,
+                              fold);
+    } else {
+      if (tid == 0) s_go = wait_wave(&sync[2 + it.wave], pl.P * pl.Tk, &sync[1], status) ? 1 : 0;
+      __syncthreads();
+      if (s_go) {
+        for (int c = tid; c < D; c += kRows)
+          fac[c] = __fdiv_rn(448.0f, fmaxf(__ldcg(vs + (int64_t)it.plane * D + c), 1e-30f));
+        __syncthreads();
+        if (s < spad) quant_v_row<D, T, true>(my_row, true, fac, v8t + (int64_t)it.plane * D * spad + s, spad);
+      }
+    }
+    __syncthreads();  // the stage and fac / red are free for the next item; s_item is visible
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -370,6 +643,79 @@ static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, 
   return kStatusOk;
 }
 
+// Work list of the single-launch quantiser: waves of P kv planes whose V bytes stay under kWaveBytes
+// (a small part of the 126 MB L2, so that a wave's V rows are still cached when its B items re-read them
+// one wave later, after the next wave's Q, K and V reads), P a divisor of B * Hkv so that all waves are
+// alike.
+constexpr int64_t kWaveBytes = 12ll << 20;
+constexpr int kWaveLag = 1;
+
+static FusedPlan fused_plan(int B, int H, int Hkv, int Sq, int Skv, int D, int elem_bytes) {
+  FusedPlan pl{};
+  const int planes = B * Hkv;
+  const int64_t plane_bytes = (int64_t)Skv * D * elem_bytes;
+  int p = (int)std::max<int64_t>(1, std::min<int64_t>(planes, kWaveBytes / std::max<int64_t>(plane_bytes, 1)));
+  while (planes % p != 0) --p;
+  pl.P = p;
+  pl.W = planes / p;
+  pl.Tk = (int)((kv_pad(Skv) + kRows - 1) / kRows);
+  pl.Tq = (Sq + kRows - 1) / kRows;
+  pl.g = H / Hkv;
+  pl.LA = 2 * p * pl.Tk + p * pl.g * pl.Tq;
+  pl.LB = p * pl.Tk;
+  pl.lag = std::min(pl.W, kWaveLag);
+  pl.total = pl.W * (pl.LA + pl.LB);
+  return pl;
+}
+
+int quant_fused_sync_ints(int B, int Hkv) { return 2 + B * Hkv; }
+
+template <int D, typename T>
+static int quant_fused_t(const void* q, const void* k, const void* v, int B, int H, int Hkv, int Sq, int Skv,
+                         Strides3 sq, Strides3 sk, Strides3 sv, float fold, int8_t* q8, float* qs, int8_t* k8,
+                         float* ks, uint8_t* v8t, float* vs, int* sync, int* status, cudaStream_t stream) {
+  if ((int64_t)B * Hkv * ((kv_pad(Skv) + kRows - 1) / kRows) * 3 + (int64_t)B * H * ((Sq + kRows - 1) / kRows) >
+      (int64_t)INT32_MAX - 4 * 148 * 32) {
+    set_error("quantiser work list of more than 2^31 items");
+    return kStatusUnsupported;
+  }
+  const FusedPlan pl = fused_plan(B, H, Hkv, Sq, Skv, D, (int)sizeof(T));
+  // vs (max via atomicMax from zero) and the work counters are zeroed together when they are adjacent
+  const size_t vs_bytes = sizeof(float) * (size_t)B * Hkv * D;
+  const size_t sync_bytes = sizeof(int) * (size_t)quant_fused_sync_ints(B, Hkv);
+  cudaError_t e;
+  if (reinterpret_cast<char*>(vs) + vs_bytes == reinterpret_cast<char*>(sync)) {
+    e = cudaMemsetAsync(vs, 0, vs_bytes + sync_bytes, stream);
+  } else {
+    e = cudaMemsetAsync(vs, 0, vs_bytes, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(sync, 0, sync_bytes, stream);
+  }
+  if (e != cudaSuccess) {
+    set_error("quantiser memset: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  // persistent grid: every CTA slot of the GPU (the work list does not rely on them all being resident)
+  constexpr int smem = 2 * stage_bytes<D>();
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaFuncSetAttribute(quant_fused_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_fused_kernel<D, T>, kRows, smem) != cudaSuccess ||
+        n < 1)
+      n = 1;
+    per_sm = n;
+  }
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
+  const int grid = (int)std::min<int64_t>(pl.total, (int64_t)per_sm * sms);
+  quant_fused_kernel<D, T><<<grid, kRows, smem, stream>>>(
+      reinterpret_cast<const T*>(q), reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), Sq, Skv, H, Hkv, sq,
+      sk, sv, fold, q8, qs, k8, ks, v8t, vs, sync, status, pl);
+  return check_launch("quant_fused");
+}
+
 // ------------------------------------------------------------------------------------------------
 // varlen offsets: check the cumulative sequence tables and derive the padded key offsets
 // ------------------------------------------------------------------------------------------------
@@ -435,6 +781,13 @@ int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides
 int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
                     const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
   SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream, sg)
+}
+
+int launch_quant_fused(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                       int D, Strides3 sq, Strides3 sk, Strides3 sv, float fold, int8_t* q8, float* qs, int8_t* k8,
+                       float* ks, uint8_t* v8t, float* vs, int* sync, int* status, cudaStream_t stream) {
+  SAGE_DISPATCH_D(D, quant_fused_t, q, k, v, B, H, Hkv, Sq, Skv, sq, sk, sv, fold, q8, qs, k8, ks, v8t, vs, sync,
+                  status, stream)
 }
 
 }  // namespace sage

@@ -39,6 +39,10 @@ SIGNATURES = {
     "sage_quant_q": (_c_i, [_c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64, _c_f, _c_p, _c_p, _c_p]),
     "sage_quant_kv": (_c_i, [_c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                              _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p]),
+    "sage_quant_sync_ints": (_c_i, [_c_i, _c_i]),
+    "sage_quant_qkv": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64,
+                              _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p,
+                              _c_p, _c_p, _c_p, _c_p]),
     "sage_attn_fwd": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i,
                              _c_i, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
     "sage_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i, _c_i]),

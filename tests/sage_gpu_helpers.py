@@ -49,6 +49,35 @@ def gpu_quant(q, k, v, layout: str, fold: float = 1.0):
     return dict(q8=q8, qs=qs, k8=k8, ks=ks, v8t=v8t, vs=vs, B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D)
 
 
+def gpu_quant_fused(q, k, v, layout: str, fold: float = 1.0):
+    """The single-launch quantiser (sage_quant_qkv) on the same buffers as gpu_quant."""
+    L = _lib.lib()
+    if layout == "HND":
+        B, H, Sq, D = q.shape
+        Hkv, Skv = k.shape[1], k.shape[2]
+    else:
+        B, Sq, H, D = q.shape
+        Skv, Hkv = k.shape[1], k.shape[2]
+    dk = L.sage_qk_row_bytes(D)
+    spad = (Skv + 31) // 32 * 32
+    dev = q.device
+    vs = torch.full((B, Hkv, D), -1.0, device=dev, dtype=torch.float32)
+    sync = torch.full((L.sage_quant_sync_ints(B, Hkv),), 99, device=dev, dtype=torch.int32)
+    q8 = torch.full((B, H, Sq, dk), 77, device=dev, dtype=torch.int8)
+    qs = torch.empty((B, H, Sq), device=dev, dtype=torch.float32)
+    k8 = torch.full((B, Hkv, spad, dk), 77, device=dev, dtype=torch.int8)
+    ks = torch.empty((B, Hkv, spad // 32), device=dev, dtype=torch.float32)
+    v8t = torch.full((B, Hkv, D, spad), 0x55, device=dev, dtype=torch.uint8)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    _lib.check(L.sage_quant_qkv(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPE_CODE[q.dtype], B, H, Hkv, Sq, Skv, D,
+                                *bsh_strides(q, layout), *bsh_strides(k, layout), *bsh_strides(v, layout), fold,
+                                q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(),
+                                vs.data_ptr(), sync.data_ptr(), status.data_ptr(), stream()), "quant_qkv")
+    torch.cuda.synchronize()
+    return dict(q8=q8, qs=qs, k8=k8, ks=ks, v8t=v8t, vs=vs, B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D,
+                status=int(status.item()), sync=sync.cpu())
+
+
 def gpu_attn_from_quant(qt: dict, out_dtype: torch.dtype, causal: bool, with_lse: bool = False):
     """sage_attn_fwd on already-quantised buffers (kernel layouts); returns out (B, Sq, H, D) and lse."""
     L = _lib.lib()

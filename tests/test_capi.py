@@ -36,11 +36,13 @@ def test_host_only_queries():
     L = _lib.lib()
     assert L.sage_abi_version() == _lib.ABI_VERSION
     assert [L.sage_qk_row_bytes(d) for d in (64, 96, 128, 256, 80)] == [64, 128, 128, 256, 0]
-    # workspace = q8 + qs + k8 + ks + v8t + vs, each part 256-byte aligned
+    # workspace = q8 + qs + k8 + ks + v8t + (vs + quantiser work counters), each part 256-byte aligned
     B, H, Hkv, Sq, Skv, D = 1, 40, 40, 32760, 32760, 128
     sp = 32768
+    assert L.sage_quant_sync_ints(B, Hkv) == 2 + B * Hkv
+    assert L.sage_quant_sync_ints(0, 4) == 0
     parts = [B * H * Sq * 128, B * H * Sq * 4, B * Hkv * sp * 128, B * Hkv * sp // 32 * 4, B * Hkv * D * sp,
-             B * Hkv * D * 4]
+             B * Hkv * D * 4 + (2 + B * Hkv) * 4]
     assert L.sage_workspace_bytes(B, H, Hkv, Sq, Skv, D) == sum((p + 255) // 256 * 256 for p in parts)
     assert L.sage_workspace_bytes(1, 2, 2, 10, 10, 80) == 0
 
@@ -60,6 +62,11 @@ def test_argument_errors_without_gpu():
     assert rc == _lib.SAGE_ERR_INVALID          # misaligned input pointer
     with pytest.raises(RuntimeError, match="invalid argument"):
         _lib.check(rc, "sage_quant_q")
+    args = [0, 1, 4, 2, 64, 64, 128] + [8] * 9 + [1.0] + [16] * 6
+    rc = L.sage_quant_qkv(16, 16, 16, *args, None, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"sync" in L.sage_last_error()   # no sync scratch
+    rc = L.sage_quant_qkv(16, 16, 16, 0, 1, 3, 2, *args[4:], 16, None, None)
+    assert rc == _lib.SAGE_ERR_UNSUPPORTED      # 3 heads over 2 kv heads
 
 
 def test_host_pipeline_planner_without_gpu():

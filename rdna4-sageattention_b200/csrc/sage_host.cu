@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <vector>
 
 #include "../../include/sage_b200.h"
 #include "sage_internal.h"
@@ -104,41 +105,63 @@ size_t slot_bytes(int B, int hg, int hkg, int Sq, int Skv, int D, size_t es) {
          align256((size_t)B * hg * Sq * 4);
 }
 
-// Chunk size in query heads when the caller passes 0: a small simulation of the three-stage pipeline
-// (copy in, compute with whole waves of CTAs, copy out) over every multiple of the group size, with
-// nominal rates for a PCIe 5.0 x16 link and the attention kernel.  The rates only rank the candidates.
+// Chunk size in query heads when the caller passes 0: a simulation of the three-stage pipeline (copy in,
+// compute, copy out, two staging slots) over every multiple of the group size.  The copies share one PCIe
+// link: alone they run at the H2D / D2H rates, together at `both` split in that ratio.  A chunk's kernels
+// take whole waves of CTAs plus a per-chunk overhead.  The constants are measured on B200 (PCIe 5.0 x16;
+// the Wan call's attention rate) and only rank the candidates: on the Wan call (B1 H40 N32760 D128)
+// 2-head chunks take 21.2 ms, 1-head chunks 22.0 ms and 8-head chunks 23.9 ms.
 int auto_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D) {
   const int G = H / Hkv;
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (nsm <= 0) nsm = 148;
-  const double link = 50e9;      // bytes/s each way
-  const double rate = 1.2e15;    // attention operations/s
-  const double launch = 20e-6;   // per-chunk launch and tail overhead, s
+  const double h2d = 51e9, d2h = 50e9, both = 88e9;  // bytes/s
+  const double rate = 1.32e15;                        // attention operations/s on a full GPU
+  const double overhead = 70e-6;                      // per chunk: quantiser launches, ramp-up, copy set-up
   const double es = 2.0;
-  const double tiles_per_head = (double)B * ((Sq + attention_rows_per_cta(D) - 1) / attention_rows_per_cta(D));
-  const double t_in_q = (double)B * Sq * D * es / link, t_in_kv = 2.0 * B * Skv * D * es / link;
-  const double t_out = (double)B * Sq * D * es / link;
-  const double t_head = 4.0 * B * Sq * (double)Skv * D / rate;   // one head's kernel time
-  const double t_wave = t_head * nsm / tiles_per_head;           // one full wave of CTAs
+  const double rows = attention_rows_per_cta(D);
+  const double tiles_per_head = (double)B * std::ceil(Sq / rows);
+  const double t_head = 4.0 * B * Sq * (double)Skv * D / rate;  // one head's kernel time on a full GPU
+  const double t_wave = t_head * nsm / tiles_per_head;          // one full wave of CTAs
+  const double q_bytes = (double)B * Sq * D * es, kv_bytes = 2.0 * B * Skv * D * es;
   int best = H;
   double best_t = 1e30;
   for (int hkg = 1; hkg <= Hkv; ++hkg) {
     const int hg = hkg * G;
     const int nch = (H + hg - 1) / hg;
-    double in_end = 0, comp_end = 0, out_end = 0, comp_prev[2] = {0, 0}, out_prev[2] = {0, 0};
-    for (int c = 0; c < nch; ++c) {
+    auto in_bytes = [&](int c) { const int hc = std::min(hg, H - c * hg); return hc * q_bytes + (hc / G) * kv_bytes; };
+    auto out_bytes = [&](int c) { return std::min(hg, H - c * hg) * q_bytes; };
+    auto comp_time = [&](int c) {
       const int hc = std::min(hg, H - c * hg);
-      const double tin = hc * t_in_q + (hc / G) * t_in_kv;
-      const double tc = launch + std::ceil(hc * tiles_per_head / nsm) * t_wave;
-      in_end = std::max(in_end, comp_prev[c & 1]) + tin;
-      comp_end = std::max(std::max(comp_end, in_end), out_prev[c & 1]) + tc;
-      out_end = std::max(out_end, comp_end) + hc * t_out;
-      comp_prev[c & 1] = comp_end;
-      out_prev[c & 1] = out_end;
+      return overhead + std::ceil(hc * tiles_per_head / nsm) * t_wave;
+    };
+    // event simulation: chunk c's copy-in needs chunk c-2's kernels done (slot reuse); its kernels need
+    // its copy-in and chunk c-2's copy-out done; its copy-out needs its kernels done
+    std::vector<double> in_done(nch, -1), comp_done(nch, -1), out_done(nch, -1);
+    int ci = 0, cc = 0, co = 0;
+    double t = 0, in_rem = -1, out_rem = -1, comp_end = -1;
+    for (int guard = 0; co < nch && guard < 8 * nch + 8; ++guard) {
+      if (in_rem < 0 && ci < nch && (ci < 2 || (comp_done[ci - 2] >= 0 && comp_done[ci - 2] <= t)))
+        in_rem = in_bytes(ci);
+      if (comp_end < 0 && cc < nch && in_done[cc] >= 0 && in_done[cc] <= t &&
+          (cc < 2 || (out_done[cc - 2] >= 0 && out_done[cc - 2] <= t)))
+        comp_end = t + comp_time(cc);
+      if (out_rem < 0 && co < nch && comp_done[co] >= 0 && comp_done[co] <= t) out_rem = out_bytes(co);
+      const bool shared = in_rem >= 0 && out_rem >= 0;
+      const double ri = shared ? both * h2d / (h2d + d2h) : h2d, ro = shared ? both * d2h / (h2d + d2h) : d2h;
+      double dt = 1e30;
+      if (in_rem >= 0) dt = std::min(dt, in_rem / ri);
+      if (out_rem >= 0) dt = std::min(dt, out_rem / ro);
+      if (comp_end >= 0) dt = std::min(dt, comp_end - t);
+      if (dt >= 1e30) break;  // nothing can run (does not happen for a consistent schedule)
+      t += dt;
+      if (in_rem >= 0 && (in_rem -= ri * dt) <= 1.0) in_done[ci++] = t, in_rem = -1;
+      if (out_rem >= 0 && (out_rem -= ro * dt) <= 1.0) out_done[co++] = t, out_rem = -1;
+      if (comp_end >= 0 && comp_end <= t * (1 + 1e-12) + 1e-12) comp_done[cc++] = t, comp_end = -1;
     }
-    if (out_end < best_t * 0.999) {
-      best_t = out_end;
+    if (co == nch && t < best_t * 0.999) {
+      best_t = t;
       best = hg;
     }
   }

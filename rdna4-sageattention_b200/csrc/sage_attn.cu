@@ -201,9 +201,11 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  int grp = blockIdx.x % p.q_groups;
-  const int bh = blockIdx.x / p.q_groups;
-  if (CAUSAL) grp = p.q_groups - 1 - grp;  // longest key ranges first
+  // Non-causal CTAs all carry the same work.  Causal CTAs are ordered by work, longest key ranges first,
+  // across all (batch, head) planes (group-major), so that the last wave holds the shortest tiles.
+  const int n_bh = (int)(gridDim.x / (unsigned)p.q_groups);
+  const int grp = CAUSAL ? p.q_groups - 1 - (int)blockIdx.x / n_bh : (int)blockIdx.x % p.q_groups;
+  const int bh = CAUSAL ? (int)blockIdx.x % n_bh : (int)blockIdx.x / p.q_groups;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int hkv = h / (p.H / p.Hkv);

@@ -201,8 +201,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Non-causal CTAs all carry the same work.  Causal CTAs are ordered by work, longest key ranges first,
-  // across all (batch, head) planes (group-major), so that the last wave holds the shortest tiles.
+  // Non-causal CTAs all carry the same work and run plane by plane.  Causal CTAs run longest key ranges
+  // first across all (batch, head) planes (group-major), so that the last wave holds the shortest tiles;
+  // measured faster than longest-first within each plane also when the planes' K / V exceed L2.
   const int n_bh = (int)(gridDim.x / (unsigned)p.q_groups);
   const int grp = CAUSAL ? p.q_groups - 1 - (int)blockIdx.x / n_bh : (int)blockIdx.x % p.q_groups;
   const int bh = CAUSAL ? (int)blockIdx.x % n_bh : (int)blockIdx.x / p.q_groups;

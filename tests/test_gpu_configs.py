@@ -112,3 +112,11 @@ def test_config4_gqa_causal_lse():
     out, lse = sageattention.sageattn(th(q), th(k), th(v), tensor_layout="HND", is_causal=True, return_lse=True)
     assert lse.shape == (4, 32, 8192) and lse.dtype == torch.float32
     _check(q, k, v, out.transpose(1, 2), [0, 31], True, lse=lse, sdpa_heads=[0, 9, 31])
+
+
+def test_long_causal_lse():
+    """A long causal call (8 planes x 40000 keys: quantised K / V of 82 MB, beyond the ones above) with LSE;
+    its CTAs run longest key ranges first across all planes."""
+    q, k, v = _inputs(6, 1, 8, 8, 40000, 128, 1.0)
+    out, lse = sageattention.sageattn(q, k, v, tensor_layout="NHD", is_causal=True, return_lse=True)
+    _check(q, k, v, out, [3], True, n_rows=24, lse=lse, sdpa_heads=[3, 7])

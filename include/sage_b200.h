@@ -157,6 +157,12 @@ int sage_attention_host(const void* q, const void* k, const void* v, int dtype, 
  * after a stalled pipeline stage, and the context is still usable. */
 int sage_selftest_wait_timeout(int* status, int limit_ms, void* stream);
 
+/* The same for the counter waits between CTAs of the single-launch quantiser (sage_quant_qkv): `words` is
+ * a device array of 2 ints (zeroed by the call: a counter that nothing increments and the abort flag).  One
+ * wait expires after limit_ms (1..2000), stores SAGE_ERR_TIMEOUT and raises the flag (words[1] = 1); a
+ * second wait then returns at once on the flag, so the kernel ends after about one limit. */
+int sage_selftest_counter_timeout(int* status, int* words, int limit_ms, void* stream);
+
 /* Synchronise `stream`, read and clear a status word (NULL = the library's own word on the current
  * device); returns the code it held (SAGE_OK when no kernel reported an error). */
 int sage_status_sync(int* status, void* stream);

@@ -114,6 +114,30 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 // ------------------------------------------------------------------------------------------------
+// Counter waits between CTAs of one grid (the single-launch quantiser): spin until *ctr >= need, read with
+// acquire semantics at GPU scope.  Bounded: after limit_ns the first waiter to give up stores
+// SAGE_ERR_TIMEOUT into *status and raises *abort_flag; every wait that sees the flag returns false at once.
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool wait_counter(const int* ctr, int need, int* abort_flag, int* status,
+                                             uint64_t limit_ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (ld_acquire(ctr) < need) {
+    if (ld_acquire(abort_flag) != 0) return false;
+    if (global_timer_ns() - t0 > limit_ns) {
+      atomicCAS(status, 0, kStatusTimeout);
+      atomicExch(abort_flag, 1);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+
 // TMA (bulk tensor copies global -> shared, completion on an mbarrier; no multicast)
 // ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {

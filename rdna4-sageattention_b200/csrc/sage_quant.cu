@@ -412,25 +412,7 @@ __device__ __forceinline__ FusedItem decode_item(int cur, const FusedPlan& pl) {
 }
 
 // sync[0]: item counter; sync[1]: abort flag; sync[2 + w]: finished V amax items of wave w.  Zero on entry.
-__device__ __forceinline__ int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool wait_wave(const int* ctr, int need, int* abort_flag, int* status) {
-  const uint64_t t0 = global_timer_ns();
-  while (ld_acquire(ctr) < need) {
-    if (ld_acquire(abort_flag) != 0) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicCAS(status, 0, kStatusTimeout);
-      atomicExch(abort_flag, 1);
-      return false;
-    }
-    __nanosleep(64);
-  }
-  return true;
-}
+// Waits use wait_counter (sage_ptx.cuh) with the pipeline's 2 s limit.
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
@@ -562,7 +544,7 @@ __global__ void __launch_bounds__(kRows) quant_fused_kernel(const T* __restrict_
       quant_q_row<D, T, true>(my_row, valid, q8 + ((int64_t)it.plane * Sq + s) * DK, qs + (int64_t)it.plane * Sq + s,
                               fold);
     } else {
-      if (tid == 0) s_go = wait_wave(&sync[2 + it.wave], pl.P * pl.Tk, &sync[1], status) ? 1 : 0;
+      if (tid == 0) s_go = wait_counter(&sync[2 + it.wave], pl.P * pl.Tk, &sync[1], status, kWaitLimitNs) ? 1 : 0;
       __syncthreads();
       if (s_go) {
         for (int c = tid; c < D; c += kRows)

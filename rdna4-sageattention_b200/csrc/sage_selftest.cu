@@ -24,9 +24,41 @@ __global__ void wait_timeout_kernel(int* status, uint64_t limit_ns, int* gave_up
   }
 }
 
+// The single-launch quantiser's counter wait, made to expire: words[0] is a counter nothing increments,
+// words[1] the abort flag.  The first wait gives up after limit_ns (status and flag set); the second sees
+// the flag and returns at once, as the later waits of a launch whose wait expired do.
+__global__ void counter_timeout_kernel(int* words, int* status, uint64_t limit_ns) {
+  if (threadIdx.x != 0) return;
+  wait_counter(&words[0], 1, &words[1], status, limit_ns);
+  wait_counter(&words[0], 1, &words[1], status, limit_ns);
+}
+
 }  // namespace sage
 
 using namespace sage;
+
+extern "C" int sage_selftest_counter_timeout(int* status, int* words, int limit_ms, void* stream) {
+  if (limit_ms < 1 || limit_ms > 2000 || words == nullptr) {
+    set_error("limit_ms %d (1..2000) and a device array of 2 ints required", limit_ms);
+    return SAGE_ERR_INVALID;
+  }
+  int* word = status != nullptr ? status : default_status_word();
+  if (word == nullptr) {
+    set_error("no status word on this device");
+    return SAGE_ERR_LAUNCH;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(words, 0, 2 * sizeof(int), st);
+  if (e == cudaSuccess) {
+    counter_timeout_kernel<<<1, 32, 0, st>>>(words, word, (uint64_t)limit_ms * 1000000ull);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    set_error("selftest launch: %s", cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  }
+  return SAGE_OK;
+}
 
 extern "C" int sage_selftest_wait_timeout(int* status, int limit_ms, void* stream) {
   if (limit_ms < 1 || limit_ms > 2000) {

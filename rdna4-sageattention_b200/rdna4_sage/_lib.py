@@ -62,6 +62,7 @@ SIGNATURES = {
                                    _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,
                                    _c_i64, _c_i64, _c_i64, _c_p, _c_i, _c_p, _c_sz, _c_p, _c_p]),
     "sage_selftest_wait_timeout": (_c_i, [_c_p, _c_i, _c_p]),
+    "sage_selftest_counter_timeout": (_c_i, [_c_p, _c_p, _c_i, _c_p]),
     "sage_status_sync": (_c_i, [_c_p, _c_p]),
 }
 ABI_VERSION = 1

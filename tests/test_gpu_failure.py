@@ -32,3 +32,23 @@ def test_selftest_rejects_bad_limits():
     L = _lib.lib()
     assert L.sage_selftest_wait_timeout(None, 0, None) == _lib.SAGE_ERR_INVALID
     assert L.sage_selftest_wait_timeout(None, 5000, None) == _lib.SAGE_ERR_INVALID
+
+
+def test_expired_counter_wait_raises_abort_flag():
+    """The single-launch quantiser's wait between CTAs: one expiry sets the status and the abort flag, and
+    the next wait returns at once on the flag (the kernel takes about one limit, not two)."""
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    word = torch.zeros(1, dtype=torch.int32, device=dev)
+    words = torch.full((2,), 7, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    assert L.sage_selftest_counter_timeout(word.data_ptr(), words.data_ptr(), 100, stream) == _lib.SAGE_OK
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert 95.0 <= ms < 160.0, ms
+    assert words.tolist() == [0, 1]
+    assert L.sage_status_sync(word.data_ptr(), stream) == _lib.SAGE_ERR_TIMEOUT
+    assert L.sage_selftest_counter_timeout(None, None, 100, None) == _lib.SAGE_ERR_INVALID

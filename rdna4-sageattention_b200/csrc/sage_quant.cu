@@ -241,6 +241,42 @@ __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x,
   quant_q_row<D, T>(row, valid, q8 + ((int64_t)bh * S + s) * DK, qs + (int64_t)bh * S + s, fold);
 }
 
+// Q for D = 128 with two threads per token row (lanes 2r and 2r + 1): each holds 64 channels, runs the six
+// butterfly stages within its half, then the last stage (pairs 64 apart) with its partner's values
+// exchanged by shuffle; the operations and their order are those of the one-thread transform, so the codes
+// are identical.  Half the registers per thread lets twice the warps share an SM.
+template <typename T>
+__global__ void __launch_bounds__(kRows) quant_q_pair_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
+                                                             float fold, int8_t* __restrict__ q8,
+                                                             float* __restrict__ qs, int bh0) {
+  constexpr int RPB = kRows / 2;  // token rows per CTA
+  const int bh = bh0 + (int)blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int half = threadIdx.x & 1;
+  const int s = blockIdx.x * RPB + (threadIdx.x >> 1);
+  const bool valid = s < S;
+  const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h + half * 64;
+  float v[64];
+  row_values<64, T>(row, valid, true, v);  // stages 1..32 on this half
+  // stage 64: half 0 keeps x[j] + x[j + 64], half 1 keeps x[j] - x[j + 64] (as fma(x[j + 64], -1, x[j]))
+  const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+#pragma unroll
+  for (int j = 0; j < 64; j += 2) {
+    const float o0 = __shfl_xor_sync(0xffffffffu, v[j], 1);
+    const float o1 = __shfl_xor_sync(0xffffffffu, v[j + 1], 1);
+    const uint64_t mine = f2_pack(v[j], v[j + 1]), other = f2_pack(o0, o1);
+    f2_unpack(half == 0 ? f2_add(mine, other) : f2_fma(mine, neg1, other), v[j], v[j + 1]);
+  }
+  float a = abs_max<64>(v);
+  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+  const float scale = __fdiv_rn(fmaxf(a, 1e-12f), 127.0f);
+  if (valid) {
+    store_codes<64>(v, scale, q8 + ((int64_t)bh * S + s) * 128 + half * 64);
+    if (half == 0) qs[(int64_t)bh * S + s] = scale / 128.0f * fold;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // K + V: one thread per key row; a warp is one 32-key K scale block
 // ------------------------------------------------------------------------------------------------
@@ -288,6 +324,59 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
   if (!inpad) return;
   const T* vrow = v + src_b * sv.b + (t0 + (valid ? s : 0)) * sv.s + (int64_t)h * sv.h;
   quant_v_row<D, T>(vrow, valid, fac, v8t + vbase + s, pitch);
+}
+
+// K + V for dense calls with D = 128, two threads per key row (lanes 2r and 2r + 1, 64 channels each; the
+// K transform as in quant_q_pair_kernel).  A 32-key scale block is the 64 threads of a warp pair: each warp
+// reduces its 16 rows, the pair exchanges its two maxima through shared memory.  Codes, scales and V bytes
+// are those of quant_kv_kernel.
+template <typename T>
+__global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
+                                                              int H, Strides3 sk, Strides3 sv,
+                                                              const float* __restrict__ vs, int8_t* __restrict__ k8,
+                                                              float* __restrict__ ks, uint8_t* __restrict__ v8t,
+                                                              int bh0) {
+  constexpr int D = 128;
+  constexpr int RPB = kRows / 2;  // key rows per CTA (two scale blocks)
+  const int bh = bh0 + (int)blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int warp = threadIdx.x >> 5;
+  const int half = threadIdx.x & 1;
+  const int s = blockIdx.x * RPB + (threadIdx.x >> 1);
+  const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
+  const int64_t pitch = spad;
+  __shared__ float fac[D];
+  __shared__ float wmax[kRows / 32];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
+  const bool valid = s < S;     // real key (rows in [S, spad) are zero padding)
+  const bool inpad = s < spad;  // row exists in the padded tensors
+  // K: this half of the row, rotated; stage 64 with the partner lane
+  const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h + half * 64;
+  float x[64];
+  row_values<64, T>(krow, valid, true, x);
+  const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+#pragma unroll
+  for (int j = 0; j < 64; j += 2) {
+    const float o0 = __shfl_xor_sync(0xffffffffu, x[j], 1);
+    const float o1 = __shfl_xor_sync(0xffffffffu, x[j + 1], 1);
+    const uint64_t mine = f2_pack(x[j], x[j + 1]), other = f2_pack(o0, o1);
+    f2_unpack(half == 0 ? f2_add(mine, other) : f2_fma(mine, neg1, other), x[j], x[j + 1]);
+  }
+  const float a = abs_max<64>(x);
+  const float wm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
+  if ((threadIdx.x & 31) == 0) wmax[warp] = wm;
+  __syncthreads();  // fac and the warp maxima
+  const float kscale = __fdiv_rn(fmaxf(fmaxf(wmax[warp & ~1], wmax[warp | 1]), 1e-12f), 127.0f);
+  if (inpad) {
+    const int64_t orow = (int64_t)bh * pitch + s;
+    store_codes<64>(x, kscale, k8 + orow * 128 + half * 64);
+    if ((threadIdx.x & 63) == 0) ks[orow / kKvBlock] = kscale;
+    // V: this half's channels to e4m3, written transposed
+    const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h + half * 64;
+    uint8_t* vout = v8t + (int64_t)bh * D * pitch + (int64_t)half * 64 * pitch + s;
+    quant_v_row<64, T>(vrow, valid, fac + half * 64, vout, pitch);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -574,8 +663,13 @@ template <int D, typename T>
 static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold, int8_t* q8, float* qs,
                      cudaStream_t stream) {
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
-    dim3 grid((S + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
-    quant_q_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs, bh0);
+    if constexpr (D == 128) {
+      dim3 grid((S + kRows / 2 - 1) / (kRows / 2), min(kMaxGridY, B * H - bh0));
+      quant_q_pair_kernel<T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs, bh0);
+    } else {
+      dim3 grid((S + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
+      quant_q_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs, bh0);
+    }
     if (check_launch("quant_q") != kStatusOk) return kStatusLaunch;
   }
   return kStatusOk;
@@ -588,6 +682,14 @@ static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides
   const T* kp = reinterpret_cast<const T*>(k);
   const T* vp = reinterpret_cast<const T*>(v);
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
+    if constexpr (D == 128) {
+      if (sg.cu == nullptr) {
+        dim3 grid2((spad + kRows / 2 - 1) / (kRows / 2), min(kMaxGridY, B * H - bh0));
+        quant_kv_pair_kernel<T><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
+        if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
+        continue;
+      }
+    }
     dim3 grid((spad + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
     if (sg.cu != nullptr)
       quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);

@@ -259,14 +259,15 @@ __global__ void __launch_bounds__(kRows) quant_q_pair_kernel(const T* __restrict
   const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h + half * 64;
   float v[64];
   row_values<64, T>(row, valid, true, v);  // stages 1..32 on this half
-  // stage 64: half 0 keeps x[j] + x[j + 64], half 1 keeps x[j] - x[j + 64] (as fma(x[j + 64], -1, x[j]))
-  const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+  // stage 64: half 0 keeps x[j] + x[j + 64], half 1 keeps x[j] - x[j + 64], both as fma(mine, +-1, other)
+  // (one rounding of the exact sum or difference, as the one-thread add and fma(b, -1, a))
+  const float sg = half == 0 ? 1.0f : -1.0f;
+  const uint64_t sgn = f2_pack(sg, sg);
 #pragma unroll
   for (int j = 0; j < 64; j += 2) {
     const float o0 = __shfl_xor_sync(0xffffffffu, v[j], 1);
     const float o1 = __shfl_xor_sync(0xffffffffu, v[j + 1], 1);
-    const uint64_t mine = f2_pack(v[j], v[j + 1]), other = f2_pack(o0, o1);
-    f2_unpack(half == 0 ? f2_add(mine, other) : f2_fma(mine, neg1, other), v[j], v[j + 1]);
+    f2_unpack(f2_fma(f2_pack(v[j], v[j + 1]), sgn, f2_pack(o0, o1)), v[j], v[j + 1]);
   }
   float a = abs_max<64>(v);
   a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
@@ -355,13 +356,13 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
   const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h + half * 64;
   float x[64];
   row_values<64, T>(krow, valid, true, x);
-  const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+  const float sg = half == 0 ? 1.0f : -1.0f;
+  const uint64_t sgn = f2_pack(sg, sg);
 #pragma unroll
   for (int j = 0; j < 64; j += 2) {
     const float o0 = __shfl_xor_sync(0xffffffffu, x[j], 1);
     const float o1 = __shfl_xor_sync(0xffffffffu, x[j + 1], 1);
-    const uint64_t mine = f2_pack(x[j], x[j + 1]), other = f2_pack(o0, o1);
-    f2_unpack(half == 0 ? f2_add(mine, other) : f2_fma(mine, neg1, other), x[j], x[j + 1]);
+    f2_unpack(f2_fma(f2_pack(x[j], x[j + 1]), sgn, f2_pack(o0, o1)), x[j], x[j + 1]);
   }
   const float a = abs_max<64>(x);
   const float wm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));

@@ -374,7 +374,7 @@ def run_ours(args):
     sq = (q.stride(0), q.stride(1), q.stride(2))
 
     def quant_fused():
-        # the single-launch quantiser (sage_attention's choice for kv lengths up to 8192)
+        # the single-launch quantiser (sage_attention's choice for kv lengths up to 6144)
         _lib.check(L.sage_quant_qkv(q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, Bq, Hq, Hq, Sq, Sq, Dq, *sq, *sq,
                                     *sq, 1.0, q8, qs, k8, ks, v8t, vs, sync, None, st), "quant_qkv")
 

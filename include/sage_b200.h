@@ -94,7 +94,7 @@ int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const flo
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D);
 
 /* The whole hot path of rdna4_sage._attention.attention (_attention.py:97-140) in one call:
- * quantisers, then attention.  The quantisers run as one sage_quant_qkv launch when Skv <= 8192 and
+ * quantisers, then attention.  The quantisers run as one sage_quant_qkv launch when Skv <= 6144 and
  * D <= 128 (where it is the faster choice) and as sage_v_amax + sage_quant_q + sage_quant_kv otherwise;
  * the outputs are identical either way.  sm_scale <= 0 selects 1/sqrt(D); any other value
  * not within 1e-6 relative of 1/sqrt(D) is folded into the Q scales as the reference does. */

@@ -139,12 +139,12 @@ static VarlenWorkspace carve_varlen(void* base, int nseq, int H, int Hkv, int to
 }
 
 // Quantiser choice of sage_attention (outputs are identical either way).  Measured on B200 with bf16
-// inputs (CUDA events, L2 flushed): the single launch is faster while a (batch, kv head) plane is short
-// (B1 H24 S4608 D128: 0.060 vs 0.071 ms; B4 H32/8 S8192: 0.202 vs 0.214 ms; B1 H40 S8192: 0.144 vs
-// 0.159 ms) and slower for long planes and for D = 256, whose two shared-memory stages leave one CTA per
-// SM (B1 H40 S32760: 0.601 vs 0.542 ms; B1 H24 S67576: 0.918 vs 0.663 ms; B2 H16 S8192 D256: 0.470 vs
-// 0.273 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
-static bool use_fused_quantiser(int Skv, int D) { return Skv <= 8192 && D <= 128; }
+// inputs (CUDA events, L2 flushed), single launch vs the three launches: faster while a (batch, kv head)
+// plane is short (B1 H24 S4608 D128: 0.058 vs 0.072 ms), even at S8192 (B1 H40: 0.144 vs 0.146 ms;
+// B4 H32/8: 0.201 vs 0.194 ms) and slower for longer planes and for D = 256, whose two shared-memory stages
+// leave one CTA per SM (B1 H40 S32760: 0.601 vs 0.499 ms; B1 H24 S67576: 0.918 vs 0.611 ms; B2 H16 S8192
+// D256: 0.470 vs 0.273 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
+static bool use_fused_quantiser(int Skv, int D) { return Skv <= 6144 && D <= 128; }
 
 // math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)
 static bool isclose_rel(double a, double b, double rel) {

@@ -12,6 +12,7 @@
 // One thread per token row: the row's 2*D bytes are contiguous, so each thread streams them with 16-byte
 // loads (every L2 sector it touches is used in full) and writes its code row with 16-byte stores.
 #include <algorithm>
+#include <atomic>
 
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -781,19 +782,27 @@ static int quant_fused_t(const void* q, const void* k, const void* v, int B, int
   }
   // persistent grid: every CTA slot of the GPU (the work list does not rely on them all being resident)
   constexpr int smem = 2 * stage_bytes<D>();
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    int n = 0;
-    if (cudaFuncSetAttribute(quant_fused_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_fused_kernel<D, T>, kRows, smem) != cudaSuccess ||
-        n < 1)
-      n = 1;
-    per_sm = n;
+  // the shared-memory opt-in is per device: set it on every launch (as the attention launcher does)
+  e = cudaFuncSetAttribute(quant_fused_kernel<D, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_error("quantiser cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
   }
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     sms = 148;
+  // CTAs per SM of this instantiation, computed once per device (racing callers store the same value)
+  static std::atomic<int> per_sm_cache[64];
+  const int di = dev >= 0 && dev < 64 ? dev : 0;
+  int per_sm = per_sm_cache[di].load(std::memory_order_relaxed);
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, quant_fused_kernel<D, T>, kRows, smem) != cudaSuccess ||
+        n < 1)
+      n = 1;
+    per_sm = n;
+    per_sm_cache[di].store(n, std::memory_order_relaxed);
+  }
   const int grid = (int)std::min<int64_t>(pl.total, (int64_t)per_sm * sms);
   quant_fused_kernel<D, T><<<grid, kRows, smem, stream>>>(
       reinterpret_cast<const T*>(q), reinterpret_cast<const T*>(k), reinterpret_cast<const T*>(v), Sq, Skv, H, Hkv, sq,

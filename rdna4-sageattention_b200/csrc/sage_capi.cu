@@ -143,7 +143,7 @@ static VarlenWorkspace carve_varlen(void* base, int nseq, int H, int Hkv, int to
 // plane is short (B1 H24 S4608 D128: 0.058 vs 0.072 ms), even at S8192 (B1 H40: 0.144 vs 0.146 ms;
 // B4 H32/8: 0.201 vs 0.194 ms) and slower for longer planes and for D = 256, whose two shared-memory stages
 // leave one CTA per SM (B1 H40 S32760: 0.601 vs 0.499 ms; B1 H24 S67576: 0.918 vs 0.611 ms; B2 H16 S8192
-// D256: 0.470 vs 0.273 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
+// D256: 0.470 vs 0.245 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
 static bool use_fused_quantiser(int Skv, int D) { return Skv <= 6144 && D <= 128; }
 
 // math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)

@@ -7,10 +7,11 @@
 // K: same rotation, one scale per 32-key block over the whole 32 x D tile, ks not divided by RB.
 // V: clamp(v * (448 / max(vs_c, 1e-30)), -448, 448) -> e4m3 (round to nearest even), vs_c the
 //    per-channel max |V|.                                                  (sage_quant.py:51-70)
-// The rotation is a fast Walsh-Hadamard transform in registers (one thread per token row, fp32
-// butterflies); it equals the reference's fp32-accumulated product with Hm up to fp32 summation order.
-// One thread per token row: the row's 2*D bytes are contiguous, so each thread streams them with 16-byte
-// loads (every L2 sector it touches is used in full) and writes its code row with 16-byte stores.
+// The rotation is a fast Walsh-Hadamard transform in registers (fp32 butterflies); it equals the
+// reference's fp32-accumulated product with Hm up to fp32 summation order.
+// One thread per token row (two for D = 128 and 256, each holding half the channels): a row's 2*D bytes
+// are contiguous, so each thread streams its part with 16-byte loads (every L2 sector it touches is used
+// in full) and writes its codes with 16-byte stores.
 #include <algorithm>
 #include <atomic>
 

@@ -72,7 +72,8 @@ __device__ __forceinline__ void fwht(float* x) {
   fwht_stage<N, 1>(x);
 }
 
-constexpr int kRows = 128;  // token rows per CTA (one per thread, 32 per warp)
+constexpr int kRows = 128;  // threads per CTA (one token row per thread in the one-thread kernels)
+constexpr int kTprD128 = 2;  // threads per token row of the split-row D = 128 kernels
 constexpr int kMaxGridY = 65535;  // (batch, head) planes per launch (the grid's y limit)
 
 // 16 bytes of a row: from global memory through the read-only path (zeros when !valid), or from a
@@ -243,51 +244,65 @@ __global__ void __launch_bounds__(kRows) quant_q_kernel(const T* __restrict__ x,
   quant_q_row<D, T>(row, valid, q8 + ((int64_t)bh * S + s) * DK, qs + (int64_t)bh * S + s, fold);
 }
 
-// Q for D = 128 and 256 with two threads per token row (lanes 2r and 2r + 1), each holding half the channels.
-// D = 128: each half runs the six butterfly stages within it, then the last stage (pairs 64 apart) with the
-// partner's values exchanged by shuffle.  D = 256: each half is one of the two independent 128-wide rotation
-// blocks.  The operations and their order are those of the one-thread transform, so the codes are identical.
-// Half the registers per thread (D = 128) or one transform fewer per row (D = 256, whose one-thread kernel
-// transforms its first block twice to hold only 128 values) is the gain.
+// Q for D = 128 and 256 with TPR threads per token row (lanes TPR*r .. TPR*r + TPR - 1, D / TPR channels each).
+// D = 128: each part runs the butterfly stages within it, then the remaining stages (pairs D/TPR, ..., 64
+// apart) with the partner lane's values exchanged by shuffle.  D = 256 (TPR = 2): each part is one of the two
+// independent 128-wide rotation blocks.  The operations and their order are those of the one-thread
+// transform, so the codes are identical.  Fewer registers per thread (D = 128) or one transform fewer per
+// row (D = 256, whose one-thread kernel transforms its first block twice to hold only 128 values) is the gain.
 template <int D>
-__device__ __forceinline__ void pair_last_stage(float* x, int half) {
+constexpr int rows_tpr() { return D == 128 ? kTprD128 : 2; }
+
+template <int D, int TPR>
+__device__ __forceinline__ void part_cross_stages(float* x, int part) {
   if constexpr (D == 128) {
-    // half 0 keeps x[j] + x[j + 64], half 1 keeps x[j] - x[j + 64], both as fma(mine, +-1, other) (one
-    // rounding of the exact sum or difference, as the one-thread add and fma(b, -1, a))
-    const float sg = half == 0 ? 1.0f : -1.0f;
-    const uint64_t sgn = f2_pack(sg, sg);
+    constexpr int PART = D / TPR;
+    // stage with partner part ^ m: the lower part keeps a + b, the upper a - b, both as fma(mine, +-1, other)
+    // (one rounding of the exact sum or difference, as the one-thread add and fma(b, -1, a))
 #pragma unroll
-    for (int j = 0; j < 64; j += 2) {
-      const float o0 = __shfl_xor_sync(0xffffffffu, x[j], 1);
-      const float o1 = __shfl_xor_sync(0xffffffffu, x[j + 1], 1);
-      f2_unpack(f2_fma(f2_pack(x[j], x[j + 1]), sgn, f2_pack(o0, o1)), x[j], x[j + 1]);
+    for (int m = 1; m < TPR; m <<= 1) {
+      const float sg = (part & m) ? -1.0f : 1.0f;
+      const uint64_t sgn = f2_pack(sg, sg);
+#pragma unroll
+      for (int j = 0; j < PART; j += 2) {
+        const float o0 = __shfl_xor_sync(0xffffffffu, x[j], m);
+        const float o1 = __shfl_xor_sync(0xffffffffu, x[j + 1], m);
+        f2_unpack(f2_fma(f2_pack(x[j], x[j + 1]), sgn, f2_pack(o0, o1)), x[j], x[j + 1]);
+      }
     }
   }
+}
+
+template <int TPR>
+__device__ __forceinline__ float part_max(float a) {
+#pragma unroll
+  for (int m = 1; m < TPR; m <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, m));
+  return a;
 }
 
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_q_pair_kernel(const T* __restrict__ x, int S, int H, Strides3 st,
                                                              float fold, int8_t* __restrict__ q8,
                                                              float* __restrict__ qs, int bh0) {
-  static_assert(D == 128 || D == 256, "two-thread rows for D = 128 and 256");
-  constexpr int HALF = D / 2;
-  constexpr int RPB = kRows / 2;  // token rows per CTA
+  static_assert(D == 128 || D == 256, "split rows for D = 128 and 256");
+  constexpr int TPR = rows_tpr<D>();
+  constexpr int PART = D / TPR;
+  constexpr int RPB = kRows / TPR;  // token rows per CTA
   const int bh = bh0 + (int)blockIdx.y;
   const int b = bh / H;
   const int h = bh - b * H;
-  const int half = threadIdx.x & 1;
-  const int s = blockIdx.x * RPB + (threadIdx.x >> 1);
+  const int part = threadIdx.x & (TPR - 1);
+  const int s = blockIdx.x * RPB + (int)threadIdx.x / TPR;
   const bool valid = s < S;
-  const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h + half * HALF;
-  float v[HALF];
-  row_values<HALF, T>(row, valid, true, v);
-  pair_last_stage<D>(v, half);
-  float a = abs_max<HALF>(v);
-  a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+  const T* row = x + (int64_t)b * st.b + (int64_t)(valid ? s : 0) * st.s + (int64_t)h * st.h + part * PART;
+  float v[PART];
+  row_values<PART, T>(row, valid, true, v);
+  part_cross_stages<D, TPR>(v, part);
+  const float a = part_max<TPR>(abs_max<PART>(v));
   const float scale = __fdiv_rn(fmaxf(a, 1e-12f), 127.0f);
   if (valid) {
-    store_codes<HALF>(v, scale, q8 + ((int64_t)bh * S + s) * D + half * HALF);
-    if (half == 0) qs[(int64_t)bh * S + s] = scale / 128.0f * fold;
+    store_codes<PART>(v, scale, q8 + ((int64_t)bh * S + s) * D + part * PART);
+    if (part == 0) qs[(int64_t)bh * S + s] = scale / 128.0f * fold;
   }
 }
 
@@ -340,25 +355,26 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
   quant_v_row<D, T>(vrow, valid, fac, v8t + vbase + s, pitch);
 }
 
-// K + V for dense calls with D = 128 and 256, two threads per key row (lanes 2r and 2r + 1, half the
-// channels each; the K transform as in quant_q_pair_kernel).  A 32-key scale block is the 64 threads of a
-// warp pair: each warp reduces its 16 rows, the pair exchanges its two maxima through shared memory.
-// Codes, scales and V bytes are those of quant_kv_kernel.
+// K + V for dense calls with D = 128 and 256, TPR threads per key row (the K transform as in
+// quant_q_pair_kernel).  A 32-key scale block is the 32 * TPR threads of TPR consecutive warps: each warp
+// reduces its rows, the warps of a block exchange their maxima through shared memory.  Codes, scales and V
+// bytes are those of quant_kv_kernel.
 template <int D, typename T>
 __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
                                                               int H, Strides3 sk, Strides3 sv,
                                                               const float* __restrict__ vs, int8_t* __restrict__ k8,
                                                               float* __restrict__ ks, uint8_t* __restrict__ v8t,
                                                               int bh0) {
-  static_assert(D == 128 || D == 256, "two-thread rows for D = 128 and 256");
-  constexpr int HALF = D / 2;
-  constexpr int RPB = kRows / 2;  // key rows per CTA (two scale blocks)
+  static_assert(D == 128 || D == 256, "split rows for D = 128 and 256");
+  constexpr int TPR = rows_tpr<D>();
+  constexpr int PART = D / TPR;
+  constexpr int RPB = kRows / TPR;  // key rows per CTA (a multiple of the 32-key block)
   const int bh = bh0 + (int)blockIdx.y;
   const int b = bh / H;
   const int h = bh - b * H;
   const int warp = threadIdx.x >> 5;
-  const int half = threadIdx.x & 1;
-  const int s = blockIdx.x * RPB + (threadIdx.x >> 1);
+  const int part = threadIdx.x & (TPR - 1);
+  const int s = blockIdx.x * RPB + (int)threadIdx.x / TPR;
   const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
   const int64_t pitch = spad;
   __shared__ float fac[D];
@@ -366,24 +382,28 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
   for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
   const bool valid = s < S;     // real key (rows in [S, spad) are zero padding)
   const bool inpad = s < spad;  // row exists in the padded tensors
-  // K: this half of the row, rotated
-  const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h + half * HALF;
-  float x[HALF];
-  row_values<HALF, T>(krow, valid, true, x);
-  pair_last_stage<D>(x, half);
-  const float a = abs_max<HALF>(x);
+  // K: this part of the row, rotated
+  const T* krow = k + (int64_t)b * sk.b + (int64_t)(valid ? s : 0) * sk.s + (int64_t)h * sk.h + part * PART;
+  float x[PART];
+  row_values<PART, T>(krow, valid, true, x);
+  part_cross_stages<D, TPR>(x, part);
+  const float a = abs_max<PART>(x);
   const float wm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
   if ((threadIdx.x & 31) == 0) wmax[warp] = wm;
   __syncthreads();  // fac and the warp maxima
-  const float kscale = __fdiv_rn(fmaxf(fmaxf(wmax[warp & ~1], wmax[warp | 1]), 1e-12f), 127.0f);
+  float bm = 0.f;
+  const int w0 = warp & ~(TPR - 1);
+#pragma unroll
+  for (int i = 0; i < TPR; ++i) bm = fmaxf(bm, wmax[w0 + i]);
+  const float kscale = __fdiv_rn(fmaxf(bm, 1e-12f), 127.0f);
   if (inpad) {
     const int64_t orow = (int64_t)bh * pitch + s;
-    store_codes<HALF>(x, kscale, k8 + orow * D + half * HALF);
-    if ((threadIdx.x & 63) == 0) ks[orow / kKvBlock] = kscale;
-    // V: this half's channels to e4m3, written transposed
-    const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h + half * HALF;
-    uint8_t* vout = v8t + (int64_t)bh * D * pitch + (int64_t)half * HALF * pitch + s;
-    quant_v_row<HALF, T>(vrow, valid, fac + half * HALF, vout, pitch);
+    store_codes<PART>(x, kscale, k8 + orow * D + part * PART);
+    if ((threadIdx.x & (32 * TPR - 1)) == 0) ks[orow / kKvBlock] = kscale;
+    // V: this part's channels to e4m3, written transposed
+    const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h + part * PART;
+    uint8_t* vout = v8t + (int64_t)bh * D * pitch + (int64_t)part * PART * pitch + s;
+    quant_v_row<PART, T>(vrow, valid, fac + part * PART, vout, pitch);
   }
 }
 
@@ -672,7 +692,8 @@ static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold
                      cudaStream_t stream) {
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
     if constexpr (D == 128 || D == 256) {
-      dim3 grid((S + kRows / 2 - 1) / (kRows / 2), min(kMaxGridY, B * H - bh0));
+      constexpr int rpb = kRows / rows_tpr<D>();
+      dim3 grid((S + rpb - 1) / rpb, min(kMaxGridY, B * H - bh0));
       quant_q_pair_kernel<D, T><<<grid, kRows, 0, stream>>>(reinterpret_cast<const T*>(q), S, H, st, fold, q8, qs,
                                                             bh0);
     } else {
@@ -693,7 +714,8 @@ static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
     if constexpr (D == 128 || D == 256) {
       if (sg.cu == nullptr) {
-        dim3 grid2((spad + kRows / 2 - 1) / (kRows / 2), min(kMaxGridY, B * H - bh0));
+        constexpr int rpb = kRows / rows_tpr<D>();
+        dim3 grid2((spad + rpb - 1) / rpb, min(kMaxGridY, B * H - bh0));
         quant_kv_pair_kernel<D, T><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
         if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
         continue;

@@ -209,6 +209,7 @@ int sage_quant_qkv(const void* q, const void* k, const void* v, int dtype, int B
                    int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
                    int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
                    float* vs, int* sync, int* status, void* stream) {
+  NvtxRange nvtx("sage_quant_qkv");
   g_error[0] = 0;
   int rc = check_common(dtype, B, Sq, H, D);
   if (rc != SAGE_OK) return rc;
@@ -238,6 +239,7 @@ int sage_quant_qkv(const void* q, const void* k, const void* v, int dtype, int B
 int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
                   const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D, int causal,
                   int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream) {
+  NvtxRange nvtx("sage_attn_fwd");
   g_error[0] = 0;
   int rc = check_common(out_dtype, B, Sq, H, D);
   if (rc != SAGE_OK) return rc;
@@ -265,6 +267,7 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
                    int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
                    int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb, int64_t oss,
                    int64_t osh, float* lse, void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  NvtxRange nvtx("sage_attention");
   g_error[0] = 0;
   const size_t need = sage_workspace_bytes(B, H, Hkv, Sq, Skv, D);
   if (need == 0) {
@@ -307,6 +310,7 @@ int sage_attention_varlen(const void* q, const void* k, const void* v, int dtype
                           int total_q, int total_k, int64_t qss, int64_t qsh, int64_t kss, int64_t ksh, int64_t vss,
                           int64_t vsh, double sm_scale, int causal, void* out, int64_t oss, int64_t osh, float* lse,
                           void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  NvtxRange nvtx("sage_attention_varlen");
   g_error[0] = 0;
   int rc = check_common(dtype, nseq, total_q, H, D);
   if (rc != SAGE_OK) return rc;

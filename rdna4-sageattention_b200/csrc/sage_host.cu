@@ -200,6 +200,7 @@ int sage_attention_host(const void* q, const void* k, const void* v, int dtype, 
                         int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out, int64_t osb,
                         int64_t oss, int64_t osh, float* lse, int heads_per_chunk, void* workspace,
                         size_t workspace_bytes, int* status, void* stream) {
+  NvtxRange nvtx("sage_attention_host");
   if (dtype != SAGE_BF16 && dtype != SAGE_F16) {
     set_error("dtype %d (SAGE_BF16 or SAGE_F16 required)", dtype);
     return SAGE_ERR_UNSUPPORTED;

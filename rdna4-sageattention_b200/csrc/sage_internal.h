@@ -4,8 +4,18 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 namespace sage {
+
+// NVTX range over a public entry point (host enqueue time), named for the call; a no-op unless a profiler
+// that records NVTX is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Geometry of the quantised tensors the kernels exchange (all per (batch, head), heads outermost):
 //   q8  [B, H,   Sq,      DK] int8   (DK = qk_row_bytes(D); columns >= D are zero)

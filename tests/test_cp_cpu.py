@@ -75,3 +75,46 @@ def test_chunk_bounds_cover_sequence():
             assert b == c
             if d > c:                       # a chunk followed by a non-empty one is 32-aligned
                 assert (b - a) % 32 == 0
+
+
+def _failing_worker(rank, world, port, results):
+    """Rank 1 fails on the host before the first collective (it never joins); rank 0 runs the CP call."""
+    import datetime
+    import time
+    sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "rdna4-sageattention_b200"), os.path.dirname(HERE)]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    try:
+        if rank == 1:
+            raise RuntimeError("injected host failure on rank 1")
+        from cp_oracle_backend import OracleBackend
+        from rdna4_sage import cp
+        S, H, D = 128, 2, 64
+        g = torch.Generator().manual_seed(3)
+        q, k, v = (torch.randn(1, S, H, D, generator=g).to(torch.bfloat16) for _ in range(3))
+        t0 = time.monotonic()
+        try:
+            cp.attention_cp(cp.shard(q, S, world, rank), cp.shard(k, S, world, rank), cp.shard(v, S, world, rank),
+                            S, backend=OracleBackend())
+            results[rank] = ("returned", time.monotonic() - t0)
+        except Exception as e:  # the collective with the missing rank must fail, not hang
+            results[rank] = ("error:" + type(e).__name__, time.monotonic() - t0)
+    except RuntimeError as e:
+        results[rank] = ("injected", str(e))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(180)
+def test_cp_rank_failure_ends_the_others_collective():
+    """A rank that fails before the V-amax all-reduce: the surviving rank's collective ends with an error
+    within the process-group timeout (3 s here) instead of waiting forever."""
+    world = 2
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    port = 29500 + (os.getpid() % 1000) + 417
+    mp.start_processes(_failing_worker, args=(world, port, results), nprocs=world, join=True, start_method="spawn")
+    assert results[1][0] == "injected"
+    status, elapsed = results[0]
+    assert status.startswith("error:"), status
+    assert elapsed < 60.0, elapsed

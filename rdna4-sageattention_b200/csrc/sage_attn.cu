@@ -16,6 +16,8 @@
 //   D = 256:     QT = 1, BN = 128; the two slots alternate between consecutive key tiles so QK^T of
 //                tile j+1 overlaps the softmax of tile j
 // With QT >= 2, slot t belongs to Q tile t.
+// Grid: one CTA per (batch, head, query group), plane by plane; causal grids run by query group across all
+// planes, longest key ranges first.
 //
 // Arithmetic per query row i and key tile (matches the reference up to the tile width):
 //   c      = fp32(sm_scale*log2e) * qs_i

@@ -236,14 +236,13 @@ def attention_rows(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarra
       s       = q8 . k8 (int32, exact in fp32)
       rowmax  = max_j(s_j) * ks_b                                        (make_sage.py:196-202)
       m_cand  = max(m, rowmax); m moves to m_cand iff (m_cand - m) * c > 8   (make_sage.py:219-225)
-    then, per tile of `block_n` keys (32 = the reference; the B200 kernel uses 128 = four blocks whose
-    lazy decisions are taken in order as above):
+    then, per tile of `block_n` keys (32 = the reference's schedule, which the B200 kernel follows block
+    for block; 128 = four blocks per step, an alternative schedule kept for comparison):
       corr    = exp2((m_old - m_new) * c); p = exp2(fma(s, c * ks_b, -c * m_new))
       l       = corr * l + sum p;  O = O * corr (only when m moved);  O += e4m3(p) . v8
       out     = O * (1/448) / l * vs                                      (make_sage_r2.py:255-268)
-    with c = fp32(sm_scale * log2e) * qs.  With block_n = 128 the only difference from the reference is
-    that the p of blocks preceding a max move inside the same tile are taken relative to the tile's final
-    max (a different fp8 rounding of the same value).  Keys >= seq_kv are masked; causal keeps key
+    with c = fp32(sm_scale * log2e) * qs.  With block_n = 128 the p of blocks preceding a max move inside the
+    same tile are taken relative to the tile's final max (a different fp8 rounding of the same value).  Keys >= seq_kv are masked; causal keeps key
     j <= i + (seq_kv - seq_q) (bottom-right, make_sage_r2.py:91-117).
 
     q8 (Sq, D) int8, qs (Sq,) f32, k8 (Skv_pad, D) int8, ks (Skv_pad/32,) f32, v8 (Skv_pad, D) uint8

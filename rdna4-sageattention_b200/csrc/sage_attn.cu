@@ -7,9 +7,9 @@
 //   warp 4*QT+1    MMA issuer (one thread): S_t = Q_t K^T with tcgen05.mma kind::i8 into TMEM (int32),
 //                  O_t += P_t V with kind::f8f6f4, P_t read from TMEM
 //   warps 0..4QT-1 softmax, one warpgroup per Q tile and one thread per query row: reads S_t from
-//                  TMEM, applies the per-32-key K scales, keeps the running max lazily (threshold 8 in
-//                  log2 units, as the reference), writes P_t = e4m3(exp2(...)) back into the S_t columns,
-//                  rescales O_t in TMEM when its max moved, and runs the epilogue
+//                  TMEM, runs the reference's per-32-key block step (lazy running max, threshold 8 in
+//                  log2 units), writes P_t = e4m3(p) back into the S_t columns, rescales O_t in TMEM
+//                  when its max moved, and runs the epilogue
 // TMEM (512 columns): S/P slots of BN columns from column 0, O_t at 256 + t*D.
 //   D = 64:      QT = 4, BN = 64 (four 128-row tiles, 16 softmax warps: 4 per SM sub-partition)
 //   D = 96, 128: QT = 2, BN = 128
@@ -19,13 +19,17 @@
 // Grid: one CTA per (batch, head, query group), plane by plane; causal grids run by query group across all
 // planes, longest key ranges first.
 //
-// Arithmetic per query row i and key tile (matches the reference up to the tile width):
+// Arithmetic per query row i and 32-key block b, in key order (the reference's tile, make_sage_r2.py:183-214):
 //   c      = fp32(sm_scale*log2e) * qs_i
-//   for each 32-key block b of the tile, in order (the reference's tile width):
-//     m moves to max(m, max_j(s_ij) * ks_b) iff that exceeds m by more than 8 / c
-//   corr   = exp2((m_old - m_new) * c), O and l rescaled only when m moved
-//   p_ij   = exp2(fma(s_ij, c * ks_b, -c * m_new)),  l = corr * l + sum_j p_ij
-//   O     += e4m3(p) . v8,   out = O * ((1/448) / l) * vs_channel
+//   m      moves to max(m, max_j(s_ij) * ks_b) iff that exceeds m by more than 8 / c
+//   k_b    = exp2((m_old - m) * c) (1 when m stayed),   l = k_b * l + sum_j p_ij
+//   p_ij   = exp2(fma(s_ij, c * ks_b, -c * m))            (m as it stands after block b)
+//   O      = k_b * O + e4m3(p_b) . v8_b,   out = O * ((1/448) / l) * vs_channel
+// In a tile where no row of a warp moves its max after the tile's first block, every block's max is
+// the tile's final max: the warp takes all p of the tile against it in one pass, and O is scaled by
+// k_0 before the tile's P.V.  Otherwise (rare after a row's first tile) the warp recomputes the tile
+// block by block, and the tile's P.V is split at every block where some row of the Q tile moved: the
+// tensor core stops there until the softmax warps have scaled their rows of O by that block's k.
 // Causal masks keep key j <= i + (Skv - Sq) (bottom-right aligned); keys >= Skv are masked.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -67,7 +71,7 @@ struct AttnCfg {
   static constexpr int SW = DK >= 128 ? 128 : 64;                     // swizzle width of a Q/K box
   static constexpr int BM = 128;
   static constexpr int BN = D == 64 ? 64 : 128;                       // keys per tile
-  static constexpr int NB = BN / 32;                                  // 32-key scale blocks per tile
+  static constexpr int NB = BN / 32;                                  // 32-key blocks per tile
   static constexpr int SLOT = BN;                                     // TMEM columns of one S slot
   static constexpr int VSW = BN;                                      // swizzle width of a V^T box row
   static constexpr int Q_TILE = BM * DK;
@@ -93,8 +97,12 @@ struct AttnCfg {
                 "setmaxnreg shares must sum to the launch allocation");
   static constexpr int O_COL = 256;
   static constexpr int TMEM_COLS = 512;
-  static constexpr int NUM_BARS = 1 + 3 * NST + 4 + 4 + 4 + 1;
-  static constexpr int SMEM_BYTES = 1024 + QT * Q_TILE + NST * (K_TILE + V_TILE) + NUM_BARS * 8 + 16;
+  // q_full; k_full, v_full, kv_empty per stage; s_full, p_full per slot; o_done, o_part, o_fix per tile;
+  // mma_drain
+  static constexpr int NUM_BARS = 1 + 3 * NST + 5 * 4 + 1;
+  static constexpr int MASK_INTS = 2 * 4;  // split masks: one word per [tile parity][Q tile], a byte per warp
+  static constexpr int SMEM_BYTES =
+      1024 + QT * Q_TILE + NST * (K_TILE + V_TILE) + NUM_BARS * 8 + 16 + MASK_INTS * 4;
   // Keep a second CTA off the SM: its tcgen05.alloc of all 512 columns would have to wait.
   static constexpr int SMEM_ALLOC = SMEM_BYTES > 120 * 1024 ? SMEM_BYTES : 120 * 1024;
 };
@@ -112,38 +120,27 @@ __device__ __forceinline__ uint32_t pack_p4(float a, float b, float c, float d) 
   return (uint32_t)pack_e4m3x2(a, b) | ((uint32_t)pack_e4m3x2(c, d) << 16);
 }
 
-// One query row's share of a 128-key tile: the lazy max update over the four 32-key blocks, then
-// p = exp2(s * c * ks_b - c * m_new) for all 128 keys, packed to e4m3 (4 keys per word, key 4w+b in
-// byte b) and summed in fp32.  MASK: keys >= lim are excluded (edge tiles only).  Returns the sum of p
-// and the new running max in m_new (the caller derives the correction factor).
-template <bool MASK, int NB>
-__device__ __forceinline__ float softmax_tile(uint32_t (&s)[NB][32], const float (&ksv)[NB], float c, float m,
-                                              int kv0, int lim, float& m_new, uint32_t (&pw)[NB * 8]) {
-  if (MASK) {
-#pragma unroll
-    for (int i = 0; i < NB; ++i)
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
-  }
-  // lazy running max, decided per 32-key block in key order as the reference's 32-key tiles do
-  m_new = m;
-#pragma unroll
-  for (int i = 0; i < NB; ++i) {
-    const int mx = max32_tree(s[i]);
-    if (!MASK || mx != INT32_MIN) {
-      const float cand = fmaxf(m_new, (float)mx * ksv[i]);
-      if (cand != -INFINITY && (cand - m_new) * c > 8.0f) m_new = cand;
-    }
-  }
-  const float negcm = m_new == -INFINITY ? 0.f : -(c * m_new);
-  const uint64_t neg2 = f2_pack(negcm, negcm);
+// p = exp2(fma(s, c*ks_b, negcm_b)) for all keys of a tile, packed to e4m3 (4 keys per word, key 4w+b in
+// byte b of word w) into pw, each block against its own negcm_b; returns the sum of the unrounded p (the
+// reference's row sum) in four fp32x2 accumulators used round robin.  SCALED: before block i > 0 the
+// accumulators are multiplied by k[i] (the correction of that block), so the result is
+// sum_i (prod_{i' > i} k[i']) * sum(p of block i); a row whose k[i > 0] are all 1 gets bit for bit the
+// unscaled sum.  MASK: keys holding INT32_MIN (masked before the call) get p = 0.
+template <bool MASK, bool SCALED, int NB>
+__device__ __forceinline__ float exp_tile(const uint32_t (&s)[NB][32], const float (&ksv)[NB], float c,
+                                          const float (&negcm)[NB], const float (&k)[NB], uint32_t (&pw)[NB * 8]) {
   const uint64_t unbias2 = f2_pack(-kMagicF, -kMagicF);
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
   for (int i = 0; i < NB; ++i) {
+    if (SCALED && i > 0) {
+      const uint64_t k2 = f2_pack(k[i], k[i]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) acc[a] = f2_mul(acc[a], k2);
+    }
     const float cts = c * ksv[i];
     const uint64_t cts2 = f2_pack(cts, cts);
+    const uint64_t neg2 = f2_pack(negcm[i], negcm[i]);
 #pragma unroll
     for (int w = 0; w < 8; ++w) {
       float pv[4];
@@ -176,6 +173,133 @@ __device__ __forceinline__ float softmax_tile(uint32_t (&s)[NB][32], const float
   return ((a0 + a1) + (a2 + a3)) + ((a4 + a5) + (a6 + a7));
 }
 
+template <int NB>
+struct BlockVals {  // per-block values passed by value (registers) to the out-of-line pass
+  float v[NB];
+};
+
+template <bool MASK, int NB>
+__device__ __noinline__ float exact_tile(uint32_t taddr, const BlockVals<NB> ksb, float c, const BlockVals<NB> mbb,
+                                         const BlockVals<NB> kbb, float l, int kv0, int lim) {
+  const float(&ksv)[NB] = ksb.v;
+  const float(&mb)[NB] = mbb.v;
+  const float(&k)[NB] = kbb.v;
+  uint32_t s[NB][32];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) tmem_ld32(taddr + i * 32, s[i]);
+  tmem_wait_ld();
+  if (MASK) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i)
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
+  }
+  float negcm[NB];
+  uint32_t pw[NB * 8];
+  float kall = k[0];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    negcm[i] = mb[i] == -INFINITY ? 0.f : -(c * mb[i]);
+    if (i > 0) kall *= k[i];
+  }
+  // rows without a move after block 0 get exactly the one-pass values (every k[i > 0] is 1)
+  l = kall * l + exp_tile<MASK, true, NB>(s, ksv, c, negcm, k, pw);
+  if constexpr (NB == 4)
+    tmem_st32(taddr, pw);
+  else
+    tmem_st16(taddr, pw);
+  return l;
+}
+
+// Returns true when the tile went through exact_tile (P is then already stored).
+template <bool MASK, int NB>
+__device__ __forceinline__ bool softmax_tile(uint32_t (&s)[NB][32], uint32_t taddr, const float (&ksv)[NB], float c,
+                                             float& m, float& l, int kv0, int lim, float (&k)[NB],
+                                             uint32_t (&pw)[NB * 8]) {
+  if (MASK) {
+#pragma unroll
+    for (int i = 0; i < NB; ++i)
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
+  }
+  // lazy running max, decided per 32-key block in key order as the reference's 32-key tiles do
+  float mb[NB];
+  float mc = m;
+  bool late = false;  // the max moved after the tile's first block
+#pragma unroll
+  for (int i = 0; i < NB; ++i) {
+    const int mx = max32_tree(s[i]);
+    k[i] = 1.0f;
+    if (!MASK || mx != INT32_MIN) {
+      const float cand = fmaxf(mc, (float)mx * ksv[i]);
+      if (cand != -INFINITY && (cand - mc) * c > 8.0f) {
+        k[i] = fast_exp2((mc - cand) * c);  // 0 for the first block of a row (m = -inf)
+        mc = cand;
+        late |= i > 0;
+      }
+    }
+    mb[i] = mc;
+  }
+  m = mc;
+  if (__any_sync(0xffffffffu, late)) {
+    BlockVals<NB> ksb, mbb, kbb;
+#pragma unroll
+    for (int i = 0; i < NB; ++i) {
+      ksb.v[i] = ksv[i];
+      mbb.v[i] = mb[i];
+      kbb.v[i] = k[i];
+    }
+    l = exact_tile<MASK, NB>(taddr, ksb, c, mbb, kbb, l, kv0, lim);
+    return true;
+  }
+  // every block's max is the tile's final max: one pass over the tile
+  float negcm[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) negcm[i] = mc == -INFINITY ? 0.f : -(c * mc);
+  l = k[0] * l + exp_tile<MASK, false, NB>(s, ksv, c, negcm, k, pw);
+  return false;
+}
+
+// O row (D fp32 columns from taddr) *= f, read-modify-write in TMEM.
+template <int D>
+__device__ __noinline__ void rescale_o(uint32_t taddr, float f) {
+#pragma unroll 1
+  for (int cc = 0; cc < D / 32; ++cc) {
+    uint32_t o[32];
+    tmem_ld32(taddr + cc * 32, o);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+    tmem_st32(taddr + cc * 32, o);
+  }
+  tmem_wait_st();
+}
+
+// Blocks 1.. of a tile's P.V when some row of the Q tile moved its max inside the tile (out of line:
+// rare): at each split block the MMAs so far are committed to o_part, and the tensor core waits (o_fix)
+// until the softmax warps have scaled their rows of O; then the rest, committed to o_done.  Block 0 has
+// been issued.  Returns the number of splits, or -1 if a wait gave up.
+template <int D, int NB>
+__device__ __noinline__ int pv_split(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_smem, uint32_t msk,
+                                     uint64_t* o_part, uint64_t* o_fix, uint64_t* o_done, int nsplit,
+                                     const WaitCtx wc) {
+  constexpr uint32_t kIdescPV = idesc_e4m3(128, D);
+  int n = 0;
+  for (int ks = 1; ks < NB; ++ks) {
+    if ((msk >> ks) & 1) {
+      tc_commit(o_part);
+      if (!mbar_wait(o_fix, (nsplit + n) & 1, wc)) return -1;
+      ++n;
+      tc_fence_after();
+    }
+    mma_f8_ts(o_tmem, p_tmem + ks * 8, smem_desc_kmajor(v_smem + ks * 32, (uint32_t)(NB * 32)), kIdescPV, 1u);
+  }
+  tc_commit(o_done);
+  return n;
+}
+
 template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -183,6 +307,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   using C = AttnCfg<D>;
   constexpr int QT = C::QT;
   constexpr int NST = C::NST;
+  constexpr int NB = C::NB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -193,12 +318,16 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   uint64_t* k_full = q_full + 1;
   uint64_t* v_full = k_full + NST;
   uint64_t* kv_empty = v_full + NST;
-  uint64_t* s_full = kv_empty + NST;
-  uint64_t* p_full = s_full + 4;
-  uint64_t* o_done = p_full + 4;
-  uint64_t* mma_drain = o_done + 4;
+  uint64_t* s_full = kv_empty + NST;  // per slot: S landed
+  uint64_t* p_full = s_full + 4;      // per slot (QT = 1) or tile: P stored
+  uint64_t* o_done = p_full + 4;      // per tile: the tile's P.V landed
+  uint64_t* o_part = o_done + 4;      // per tile: the P.V part before a split landed
+  uint64_t* o_fix = o_part + 4;       // per tile: O scaled at a split
+  uint64_t* mma_drain = o_fix + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_drain + 1);
   int* cta_abort = reinterpret_cast<int*>(tmem_slot + 1);
+  // split masks: word [parity][tile], byte wq = that warp's blocks (bits 1..NB-1) where some row moved its max
+  volatile uint32_t* split_mask = reinterpret_cast<volatile uint32_t*>(cta_abort + 3);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -253,6 +382,8 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&o_part[i], 1);
+      mbar_init(&o_fix[i], 4);
     }
     mbar_init(mma_drain, 1);
     *cta_abort = 0;
@@ -314,6 +445,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     if (lane == 0 && n_tiles > 0) {
       constexpr uint32_t kIdescQK = idesc_i8(128, C::BN);
       constexpr uint32_t kIdescPV = idesc_e4m3(128, D);
+      int nsplit[QT];
+#pragma unroll
+      for (int t = 0; t < QT; ++t) nsplit[t] = 0;
       auto issue_s = [&](int j, int t, int slot) {
         const int st = j % NST;
 #pragma unroll
@@ -326,15 +460,37 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         }
         tc_commit(&s_full[slot]);
       };
-      auto issue_pv = [&](int j, int t, int slot) {
+      // O_t += P.V for the 32-key blocks [b0, b1) of tile j, P read from `slot`
+      auto issue_pv = [&](int j, int t, int slot, int b0, int b1) {
         const int st = j % NST;
-#pragma unroll
-        for (int ks = 0; ks < C::NB; ++ks) {
+        for (int ks = b0; ks < b1; ++ks) {
           const uint64_t bd = smem_desc_kmajor(smem_u32(sV + st * C::V_TILE) + ks * 32, C::VSW);
           mma_f8_ts(tmem + C::O_COL + t * D, tmem + slot * C::SLOT + ks * 8, bd, kIdescPV,
                     (j > 0 || ks > 0) ? 1u : 0u);
         }
-        tc_commit(&o_done[t]);
+      };
+      // P.V of tile j, split at every block where some row of the Q tile moved its max (the softmax scales
+      // O between the parts); commits o_done[t] once the whole tile is in
+      auto pv_tile = [&](int j, int t, int slot) -> bool {
+        issue_pv(j, t, slot, 0, 1);  // no split precedes block 1: the mask read overlaps this MMA
+        const uint32_t words = split_mask[(j & 1) * 4 + t];
+        if (words == 0) {
+          const int st = j % NST;
+#pragma unroll
+          for (int ks = 1; ks < NB; ++ks) {
+            const uint64_t bd = smem_desc_kmajor(smem_u32(sV + st * C::V_TILE) + ks * 32, C::VSW);
+            mma_f8_ts(tmem + C::O_COL + t * D, tmem + slot * C::SLOT + ks * 8, bd, kIdescPV, 1u);
+          }
+          tc_commit(&o_done[t]);
+          return true;
+        }
+        const uint32_t msk = (words | (words >> 8) | (words >> 16) | (words >> 24)) & 0xffu;
+        const int n = pv_split<D, NB>(tmem + C::O_COL + t * D, tmem + slot * C::SLOT,
+                                      smem_u32(sV + (j % NST) * C::V_TILE), msk, &o_part[t], &o_fix[t], &o_done[t],
+                                      nsplit[t], wc);
+        if (n < 0) return false;
+        nsplit[t] += n;
+        return true;
       };
       bool ok = mbar_wait(q_full, 0, wc) && mbar_wait(&k_full[0], 0, wc);
       if (ok) {
@@ -359,7 +515,10 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
               break;
             }
             tc_fence_after();
-            issue_pv(j, t, t);
+            if (!pv_tile(j, t, t)) {
+              tiles_ok = false;
+              break;
+            }
             if (t == QT - 1) tc_commit(&kv_empty[st]);
             if (more) issue_s(j + 1, t, t);
           }
@@ -372,7 +531,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
           }
           if (!mbar_wait(&v_full[st], ph, wc) || !mbar_wait(&p_full[j & 1], (j >> 1) & 1, wc)) break;
           tc_fence_after();
-          issue_pv(j, 0, j & 1);
+          if (!pv_tile(j, 0, j & 1)) break;
           tc_commit(&kv_empty[st]);
         }
       }
@@ -389,14 +548,87 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
     const int row = wq * 32 + lane;
     const int q_row = q0 + t * 128 + row;
     const uint32_t tl = tmem + ((uint32_t)(wq * 32) << 16);
+    const uint32_t to = tl + C::O_COL + t * D;
     const float qsr = __ldg(p.qs + q_off + min(q_row, Sq - 1));
     const float c = p.sm_log2e * qsr;
     const float* ksb = p.ks + ks_off;
     const int last_key = CAUSAL ? q_row + off : 0x7fffffff;
+    constexpr unsigned FULL = 0xffffffffu;
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    constexpr int NB = C::NB;
+    // Splits of the previous tile.  With QT >= 2 the next S is issued only after the whole P.V of the
+    // previous tile, so a warp meets a pending split only while it waits for that S (or for the P.V): it
+    // tests o_part there and serves the split.  With QT = 1 the next S is issued before the previous
+    // P.V, so the warp settles the previous tile's splits before it announces the next P.
+    int pend_j = -1;     // tile whose P.V may still be split (-1: none)
+    int pend_mask = -1;  // its split blocks not served yet (-1: not read yet)
+    int nsplit = 0;      // splits served so far (the o_part / o_fix phases)
+    float kp[NB];        // that tile's per-block corrections
+#pragma unroll
+    for (int i = 0; i < NB; ++i) kp[i] = 1.0f;
+    // split points of tile pend_j: each warp stored its mask before arriving on p_full (acquired here)
+    auto read_mask = [&]() -> bool {
+      const int ps = QT >= 2 ? t : (pend_j & 1);
+      const uint32_t pp = QT >= 2 ? (pend_j & 1) : ((pend_j >> 1) & 1);
+      if (!__all_sync(FULL, mbar_test_wait(&p_full[ps], pp))) return false;
+      const uint32_t words = split_mask[(pend_j & 1) * 4 + t];
+      pend_mask = (int)((words | (words >> 8) | (words >> 16) | (words >> 24)) & 0xfeu);
+      pend_mask = __shfl_sync(FULL, pend_mask, 0);
+      return true;
+    };
+    // serve one split if the tensor core has stopped at it (never suspends the warp); warp-uniform
+    auto serve_one = [&]() {
+      if (pend_j < 0 || !__all_sync(FULL, mbar_test_wait(&o_part[t], nsplit & 1))) return;
+      if (pend_mask < 0 && !read_mask()) return;
+      ++nsplit;
+      tc_fence_after();
+      const int bb = __ffs(pend_mask) - 1;
+      pend_mask &= pend_mask - 1;
+      float f = 1.0f;
+#pragma unroll
+      for (int i = 1; i < NB; ++i)
+        if (i == bb) f = kp[i];
+      if (__any_sync(FULL, f != 1.0f)) rescale_o<D>(to, f);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_fix[t]);
+    };
+    // bounded wait for a barrier phase (each lane polls as in mbar_wait); in between, the warp serves
+    // pending splits (warp-uniform)
+    auto wait_s = [&](uint64_t* bar, uint32_t parity) -> bool {
+      if (__all_sync(FULL, mbar_try_wait(bar, parity))) return true;
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t n = 1;; ++n) {
+        // a pending split holds this wait up: it is looked for once the wait has lasted a microsecond
+        if ((n & 3u) == 0 && __any_sync(FULL, global_timer_ns() - t0 > 1000)) serve_one();
+        if (__all_sync(FULL, mbar_try_wait(bar, parity))) return true;
+        if ((n & 63u) == 0) {
+          if (__any_sync(FULL, aborted(wc))) return false;
+          if (__any_sync(FULL, global_timer_ns() - t0 > wc.limit_ns)) {
+            if (lane == 0) raise_timeout(wc, bar, parity);
+            return false;
+          }
+        }
+      }
+    };
+    // QT = 1: settle the previous tile's splits (bounded)
+    auto drain = [&]() -> bool {
+      const uint64_t t0 = global_timer_ns();
+      for (uint32_t n = 1; pend_j >= 0; ++n) {
+        if (pend_mask < 0) read_mask();
+        if (pend_mask == 0) break;
+        serve_one();
+        if ((n & 63u) == 0) {
+          if (__any_sync(FULL, aborted(wc))) return false;
+          if (__any_sync(FULL, global_timer_ns() - t0 > wc.limit_ns)) {
+            if (lane == 0) raise_timeout(wc);
+            return false;
+          }
+        }
+      }
+      return true;
+    };
     float ksn[NB];  // K scales of the next tile, loaded one iteration ahead
 #pragma unroll
     for (int i = 0; i < NB; ++i) ksn[i] = i < nkb ? __ldg(ksb + i) : 0.f;
@@ -411,56 +643,66 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
         const int kb = (j + 1) * NB + i;
         ksn[i] = kb < nkb ? __ldg(ksb + kb) : 0.f;
       }
-      if (!mbar_wait(&s_full[slot], sph, wc)) {
+      if (!wait_s(&s_full[slot], sph)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const uint32_t ts = tl + slot * C::SLOT;
       uint32_t s[NB][32];
 #pragma unroll
-      for (int i = 0; i < NB; ++i) tmem_ld32(tl + slot * C::SLOT + i * 32, s[i]);
+      for (int i = 0; i < NB; ++i) tmem_ld32(ts + i * 32, s[i]);
       tmem_wait_ld();
-      const bool need_mask = (kv0 + C::BN > Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key);
+      // warp-uniform choice: the masked path is exact for unmasked rows too
+      const bool need_mask = __any_sync(FULL, (kv0 + C::BN > Skv) || (CAUSAL && kv0 + C::BN - 1 > last_key));
       const int lim = min(Skv, CAUSAL ? last_key + 1 : Skv);  // keys < lim are kept
       uint32_t pw[NB * 8];
-      float sum;
-      float m_new;
-      if (need_mask)
-        sum = softmax_tile<true, NB>(s, ksv, c, m, kv0, lim, m_new, pw);
-      else
-        sum = softmax_tile<false, NB>(s, ksv, c, m, kv0, lim, m_new, pw);
-      const bool need = m_new != m;
-      const float corr = need ? fast_exp2((m - m_new) * c) : 1.0f;
-      l = corr * l + sum;
-      if constexpr (NB == 4)
-        tmem_st32(tl + slot * C::SLOT, pw);
-      else
-        tmem_st16(tl + slot * C::SLOT, pw);
-      if (__any_sync(0xffffffffu, need && j > 0)) {
-        // the previous P.V of this tile must have landed before O is rescaled
-        if (!mbar_wait(&o_done[t], (j - 1) & 1, wc)) {
+      float kb[NB];
+      const bool stored = need_mask ? softmax_tile<true, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw)
+                                    : softmax_tile<false, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw);
+      // a move at the tile's first block scales the O of the earlier tiles before this tile's P.V
+      if (__any_sync(FULL, j > 0 && kb[0] != 1.0f)) {
+        if (!wait_s(&o_done[t], (j - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t o[32];
-          tmem_ld32(tl + C::O_COL + t * D + cc * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-          tmem_st32(tl + C::O_COL + t * D + cc * 32, o);
+        rescale_o<D>(tl + C::O_COL + t * D, kb[0]);
+      }
+      if constexpr (QT == 1) {
+        if (!drain()) {
+          ok = false;
+          break;
         }
       }
+      if (!stored) {
+        if constexpr (NB == 4)
+          tmem_st32(ts, pw);
+        else
+          tmem_st16(ts, pw);
+      }
+      // blocks after the first whose max moved in some row of this warp: the P.V is split there
+      int bits = 0;
+#pragma unroll
+      for (int i = 1; i < NB; ++i) bits |= (kb[i] != 1.0f) ? (1 << i) : 0;
+      const int wmask = __reduce_or_sync(FULL, bits);
+      if (lane == 0)
+        reinterpret_cast<volatile uint8_t*>(split_mask)[((j & 1) * 4 + t) * 4 + wq] = (uint8_t)wmask;
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[QT >= 2 ? t : slot]);
-      m = m_new;
+      pend_j = j;
+      pend_mask = -1;
+#pragma unroll
+      for (int i = 0; i < NB; ++i) kp[i] = kb[i];
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok && n_tiles > 0) ok = mbar_wait(&o_done[t], (n_tiles - 1) & 1, wc);
+    // A parity wait must not run two phases ahead of its barrier.  With QT >= 2 the last S was issued
+    // after the previous tile's P.V, so that one has landed; with QT = 1 it was issued before it, so the
+    // previous tile's P.V is awaited first.
+    if (ok && QT == 1 && n_tiles > 1) ok = wait_s(&o_done[t], (n_tiles - 2) & 1);
+    if (ok && n_tiles > 0) ok = wait_s(&o_done[t], (n_tiles - 1) & 1);
     if (ok) {
       tc_fence_after();
       // a row with no keys (an empty varlen key sequence) gets zeros
@@ -472,7 +714,7 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[32];
         if (n_tiles > 0) {
-          tmem_ld32(tl + C::O_COL + t * D + cc * 32, o);
+          tmem_ld32(to + cc * 32, o);
           tmem_wait_ld();
         } else {
 #pragma unroll
@@ -596,6 +838,21 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   p.out_f16 = a.out_dtype == 1;
   auto kern = sage_attn_kernel<D, CAUSAL>;
+  if constexpr (C::REBALANCE) {
+    // setmaxnreg moves registers between warpgroups inside the allocation the CTA was launched with; a
+    // build allocating other than REGS_LAUNCH per thread would make the softmax's increase wait forever
+    static int regs = -1;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) regs = fa.numRegs;
+    });
+    if (regs != C::REGS_LAUNCH) {
+      set_error("attention kernel built with %d registers per thread; its setmaxnreg split needs %d", regs,
+                C::REGS_LAUNCH);
+      return kStatusLaunch;
+    }
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
   if (e != cudaSuccess) {
     set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -610,6 +867,18 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   }
   return kStatusOk;
 }
+
+#ifdef SAGE_DEBUG
+// The attention kernels' expired-wait record (see record_wait); cleared by the read.
+extern "C" int sage_debug_attn_wait_record(int* out5) {
+  int rec[5] = {0, 0, 0, 0, 0};
+  if (cudaMemcpyFromSymbol(rec, g_wait_record, sizeof(rec)) != cudaSuccess) return kStatusLaunch;
+  const int zero[5] = {0, 0, 0, 0, 0};
+  if (cudaMemcpyToSymbol(g_wait_record, zero, sizeof(zero)) != cudaSuccess) return kStatusLaunch;
+  for (int i = 0; i < 5; ++i) out5[i] = rec[i];
+  return kStatusOk;
+}
+#endif
 
 int attention_rows_per_cta(int D) {
   switch (D) {

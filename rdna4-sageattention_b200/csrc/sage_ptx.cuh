@@ -72,6 +72,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a phase (never suspends the thread, unlike try_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Shared abort state of one CTA plus the launch-wide status word in global memory.
 struct WaitCtx {
   volatile int* cta_abort;   // shared memory: set when any wait of this CTA gave up
@@ -83,7 +98,25 @@ __device__ __forceinline__ bool aborted(const WaitCtx& w) {
   return *w.cta_abort != 0 || *reinterpret_cast<volatile int*>(w.status) != 0;
 }
 
-__device__ __forceinline__ void raise_timeout(const WaitCtx& w) {
+#ifdef SAGE_DEBUG
+// Debug builds record the first wait of a launch that expired: {1, shared-memory address of the barrier
+// (0 for other waits), parity, block, thread}.  One record per translation unit (no relocatable device
+// code), read through that unit's sage_debug_* accessor.
+static __device__ int g_wait_record[5];
+__device__ __forceinline__ void record_wait(const void* bar, uint32_t parity) {
+  if (atomicCAS(&g_wait_record[0], 0, 1) == 0) {
+    g_wait_record[1] = bar != nullptr ? (int)smem_u32(bar) : 0;
+    g_wait_record[2] = (int)parity;
+    g_wait_record[3] = (int)blockIdx.x;
+    g_wait_record[4] = (int)threadIdx.x;
+  }
+}
+#else
+__device__ __forceinline__ void record_wait(const void*, uint32_t) {}
+#endif
+
+__device__ __forceinline__ void raise_timeout(const WaitCtx& w, const void* bar = nullptr, uint32_t parity = 0) {
+  record_wait(bar, parity);
   *w.cta_abort = 1;
   atomicCAS(w.status, 0, kStatusTimeout);
 }
@@ -97,7 +130,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if ((++n & 63u) == 0) {
       if (aborted(w)) return false;
       if (global_timer_ns() - t0 > w.limit_ns) {
-        raise_timeout(w);
+        raise_timeout(w, bar, parity);
         return false;
       }
     }

@@ -41,6 +41,6 @@ class OracleBackend:
                 hk = h // g
                 o, _ = O.attention_rows(q8n[b, h, :, :D], qsn[b, h], k8n[b, hk, :, :D], ksn[b, hk],
                                         np.ascontiguousarray(v8n[b, hk].T), vsn[b, hk], np.arange(Sq), Sq, Skv,
-                                        False, block_n=128)
+                                        False, block_n=32)
                 res[b, :, h] = o
         out.copy_(torch.from_numpy(res).to(out.dtype))

@@ -1,8 +1,9 @@
 """Attention kernel parity on the GPU.
 
 1. Kernel only: the oracle's quantised tensors go through sage_attn_fwd and the output is compared with
-   the oracle's emulation of the same schedule (128-key tiles, per-32-key lazy max) and of the
-   reference's schedule (32-key tiles).
+   the oracle's emulation of the reference's schedule (32-key blocks, each block's p against the running
+   max as it stands after that block), which the kernel follows block for block: the only differences
+   left are fp32 summation order and the exp2 unit's last bits.
 2. Full path: torch.ops.rdna4_sage.attention (quantisers + kernel) against the emulation of the
    reference's arithmetic (mean relative L1 <= 1e-2) and against fp32 attention (cosine).
 3. The reference's own kernel cases (tests/test_attention.py:11-30 of the reference): cosine > 0.998
@@ -20,8 +21,8 @@ from sage_gpu_helpers import (cos, gpu_attn_from_quant, make_qkv, oracle_quant, 
 
 pytestmark = pytest.mark.gpu
 
-REL_L1_REFERENCE = 1e-2     # vs the emulation of the reference's 32-key schedule
-REL_L1_SCHEDULE = 2e-3      # vs the emulation of the kernel's own schedule (same fp8 roundings)
+REL_L1_REFERENCE = 1e-2     # full path vs the emulation of the reference arithmetic
+REL_L1_KERNEL = 1e-5        # kernel only vs the same emulation on the same quantised tensors (measured <= 4e-7)
 LSE_TOL = 1e-3              # kernel LSE vs emulated LSE (natural log)
 
 
@@ -63,13 +64,11 @@ def test_kernel_only_matches_emulation(case, out_dtype):
     qt.update(B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D)
     out, lse = gpu_attn_from_quant(qt, TORCH_DT[out_dtype], causal, with_lse=True)
     rows = np.arange(Sq)
-    emu128, lse128 = _emulate(qn, kn, vn, None, causal, rows, 128, out_dtype)
-    emu32, _ = _emulate(qn, kn, vn, None, causal, rows, 32, out_dtype)
+    emu, emu_lse = _emulate(qn, kn, vn, None, causal, rows, 32, out_dtype)
     got = out.float().cpu().numpy()
     assert np.isfinite(got).all()
-    assert rel_l1(got, emu128) < REL_L1_SCHEDULE, rel_l1(got, emu128)
-    assert rel_l1(got, emu32) < REL_L1_REFERENCE, rel_l1(got, emu32)
-    np.testing.assert_allclose(lse.cpu().numpy(), lse128, atol=LSE_TOL, rtol=0)
+    assert rel_l1(got, emu) < REL_L1_KERNEL, rel_l1(got, emu)
+    np.testing.assert_allclose(lse.cpu().numpy(), emu_lse, atol=LSE_TOL, rtol=0)
 
 
 def _fp32_ref(q, k, v, layout, causal, scale=None):

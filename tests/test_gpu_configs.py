@@ -17,6 +17,8 @@ pytestmark = pytest.mark.gpu
 
 COS_MIN = 0.999
 REL_L1_MAX = 1e-2
+REL_L1_EXACT = 1e-5   # the kernel against the emulation of the reference's schedule on the same rows
+COS_TRACK = 1e-6      # |cos(kernel) - cos(emulation)| against fp32 attention on the same rows
 LSE_TOL = 1e-3
 
 
@@ -74,12 +76,16 @@ def _check(q, k, v, out_nhd, heads, causal, n_rows=48, lse=None, sdpa_heads=None
     c_emu, c_got = cos(emu, ref_rows), cos(got, ref_rows)
     print(f"cos kernel {c:.6f} (sampled rows {c_got:.6f}, emulation {c_emu:.6f}), rel-L1 vs emulation {r:.2e}")
     assert r <= REL_L1_MAX, r
+    # the kernel follows the reference's 32-key block schedule: on the same rows it matches the emulation to
+    # fp32 summation order, so it reaches the same cosine against fp32 attention (no slack beyond that)
+    assert r <= REL_L1_EXACT, r
+    assert abs(c_got - c_emu) <= COS_TRACK, (c_got, c_emu)
     if c_emu >= COS_MIN:
         assert c >= COS_MIN, c
     else:
-        # the reference arithmetic itself misses the bound on these inputs (K outlier channels): the kernel
-        # must then track it, and meet the reference's own test bound (tests/test_attention.py:54)
-        assert c >= 0.998 and c_got >= c_emu - 2e-4, (c, c_got, c_emu)
+        # the reference arithmetic itself misses the bound on these inputs (K outlier channels scaled x20 share
+        # int8 K blocks): the kernel then meets the reference's own test bound (tests/test_attention.py:54)
+        assert c >= 0.998, (c, c_got, c_emu)
     if lse is not None:
         got_lse = np.stack([lse[b, h, rows].cpu().numpy() for b in range(B) for h in heads])
         err = np.abs(got_lse - emu_lse).max()

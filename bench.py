@@ -1,6 +1,6 @@
 """Benchmark of the SageAttention hot path on B200: the Wan-2.1-14B 480p self-attention call.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--strong]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--weak]
 
 One step = one sageattention.sageattn call (V amax, Q quantiser, K+V quantiser, int8/fp8 attention) on
 B=1, H=40, N=32760, D=128, bf16, NHD, K ~ N(0,1) + per-channel offset N(0, std 2).  Inputs (1.0 GB) are
@@ -10,14 +10,15 @@ Prints one JSON line (rank 0):
   value      effective TOPS (4*B*H*N^2*D / time) of the whole job, inputs resident in HBM, CUDA events
   e2e        same metric through the public host-memory API (rdna4_sage.attention_host) with pinned host
              inputs copied in and the output copied out inside every step (copies overlapped with the
-             kernels chunk by chunk); the unpipelined copy + sageattn + copy sequence is reported beside it
+             kernels chunk by chunk); the unpipelined copy + attention + copy sequence is reported beside it
   roofline   the attention kernel timed alone (CUDA events around sage_attn_fwd) against the dense
              8-bit tensor peak = 2 x the measured bf16 cuBLAS peak in MEASURED_PEAKS.json
-  cpu_baseline  the reference's CPU path for this call (torch SDPA in bf16 on the host cores, the route
-             the reference takes off-GPU) on a head subset, scaled by operations
-N > 1 (torchrun, one rank per GPU): each rank runs its own (batch, head) units with no collective
-(weak scaling: global batch = N Wan calls); --strong instead splits the 40 heads of one call.
---impl reference times only the CPU path (rank 0; other ranks exit 0).
+  cpu_baseline  the reference's own CPU path for this call (sageattention.sageattn on CPU tensors, installed
+             unmodified in baseline/_ref: torch SDPA in bf16 on the host cores), full calls, timed in a separate
+             process (the --impl reference arm)
+N > 1 (torchrun, one rank per GPU): the heads of ONE call are split over the ranks in whole GQA groups
+(rdna4_sage.attention_shard; strong scaling, no collective); --weak instead gives every rank its own call.
+--impl reference times only the reference's CPU path (rank 0; other ranks exit 0).
 """
 from __future__ import annotations
 
@@ -32,8 +33,10 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "rdna4-sageattention_b200"))
-sys.path.insert(0, ROOT)
+PKG = os.path.join(ROOT, "rdna4-sageattention_b200")
+# The reference installed offline (pip --target baseline/_ref /root/reference): it ships packages named
+# like this repo's (sageattention, rdna4_sage), so the reference arm runs in a process that imports only it.
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 import torch  # noqa: E402
 
@@ -124,30 +127,24 @@ def make_inputs(device, b=B, h=H, n=N, d=D, seed=0):
     return q, k, v
 
 
-def cpu_baseline(seconds_target=12.0):
-    """The reference's CPU path (oracle restatement of src/rdna4_sage/__init__.py:44-58) on a head subset."""
-    from oracle import sage_oracle as O
-
-    _use_all_host_threads()
-    heads = 1
-    q, k, v = make_inputs("cpu", h=heads)
-    t0 = time.perf_counter()
-    O.sdpa_fallback(q, k, v, "NHD", False, None, None)
-    one = time.perf_counter() - t0
-    reps = max(1, min(8, int(seconds_target / max(one, 1e-3))))
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
-    dt = (time.perf_counter() - t0) / reps
-    return {"value": ops_per_call(h=heads) / dt / 1e12, "unit": "TOPS", "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{heads} of {H} heads (B=1 N={N} D={D} bf16 NHD) x {reps} through the reference's SDPA "
-                      f"fallback on CPU; {dt * 1e3:.0f} ms per head-call, scaled by operations "
-                      f"(full call ~ {dt * H:.1f} s)"}
+def cpu_baseline():
+    """The reference's own CPU path for this call, timed in a separate process (the --impl reference arm with a
+    small number of full calls): returns its cpu_baseline object, or None when it cannot run."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "reference", "--steps", "2", "--warmup", "1",
+           "--sample"]
+    env = dict(os.environ, RANK="0", WORLD_SIZE="1")
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        for ln in r.stdout.splitlines()[::-1]:
+            if ln.startswith("{"):
+                return json.loads(ln).get("cpu_baseline")
+    except (OSError, subprocess.TimeoutExpired, ValueError):
+        pass
+    return None
 
 
 def _use_all_host_threads():
-    """torchrun sets OMP_NUM_THREADS=1 per process; the CPU leg uses every core this process may run on."""
+    """torchrun sets OMP_NUM_THREADS=1 per process; the CPU path uses every core this process may run on."""
     try:
         n = len(os.sched_getaffinity(0))
     except AttributeError:
@@ -156,44 +153,77 @@ def _use_all_host_threads():
 
 
 def run_reference(args):
+    """The reference's own public API on the host cores: sageattention.sageattn on CPU tensors of the full Wan
+    call, which the reference routes to torch SDPA (src/sageattention/core.py:47-63 ->
+    src/rdna4_sage/__init__.py:44-58), from the unmodified install in baseline/_ref.  Rank 0 only.  Each step
+    is one whole call; when K calls would run past four minutes fewer are timed (the line says how many).
+    Without the install it times the oracle's restatement of the same route (kind "port")."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import sage_oracle as O
-
     _use_all_host_threads()
+    kind = "reference"
+    if os.path.isdir(os.path.join(REF_DIR, "sageattention")):
+        sys.path.insert(0, REF_DIR)
+        import sageattention as ref_api
 
-    heads = 1
-    q, k, v = make_inputs("cpu", h=heads)
-    for _ in range(args.warmup):
-        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+        assert os.path.dirname(os.path.dirname(os.path.abspath(ref_api.__file__))) == REF_DIR, ref_api.__file__
+
+        def call(q, k, v):
+            return ref_api.sageattn(q, k, v, tensor_layout="NHD")
+    else:
+        sys.path.insert(0, ROOT)
+        from oracle import sage_oracle as O
+
+        kind = "port"
+
+        def call(q, k, v):
+            return O.sdpa_fallback(q, k, v, "NHD", False, None, None)
+
+    q, k, v = make_inputs("cpu")
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        O.sdpa_fallback(q, k, v, "NHD", False, None, None)
-    dt = (time.perf_counter() - t0) / args.steps
-    value = ops_per_call(h=heads) / dt / 1e12
+    for _ in range(max(1, args.warmup)):
+        call(q, k, v)
+    one = (time.perf_counter() - t0) / max(1, args.warmup)
+    steps = args.steps if one * args.steps <= 240.0 else max(1, int(240.0 / one))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call(q, k, v)
+    dt = (time.perf_counter() - t0) / steps
+    value = ops_per_call() / dt / 1e12
+    cores = torch.get_num_threads()
+    sample = (f"{steps} full calls (B=1 H={H} N={N} D={D} bf16 NHD) through "
+              + ("the reference's sageattention.sageattn on CPU tensors (its SDPA route), installed unmodified "
+                 "in baseline/_ref" if kind == "reference" else "the oracle's restatement of the reference's SDPA route")
+              + f"; {dt:.2f} s per call")
     line = {"metric": METRIC, "value": value, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 * H / heads,
+            "steps": steps, "steps_requested": args.steps, "warmup": max(1, args.warmup), "ms_per_step": dt * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": N, "parallelism": "host cores"},
-            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{heads} of {H} heads per step through the reference's SDPA fallback on "
-                                       f"CPU (torch bf16 SDPA), ms_per_step scaled to the full 40-head call"},
+            "cpu_baseline": {"value": value, "unit": "TOPS", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
+def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks, heads=None):
     """Time the public API with pinned host inputs copied in and the output copied out every step.
 
     Headline: rdna4_sage.attention_host (one C-ABI call; chunks of heads copied in, attended and copied
     out on three streams, so the copies overlap the kernels).  Also timed: the unpipelined sequence a
-    caller of the device API writes (copy Q, K, V in; sageattention.sageattn; copy the output out)."""
+    caller of the device API writes (copy Q, K, V in; the attention call; copy the output out).
+    heads = (h0, h1): this rank's share of a call split by heads; its host views are copied in and its
+    output heads copied back into the call's host output."""
     import rdna4_sage
     import sageattention
 
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
     hout = torch.empty(q.shape, dtype=q.dtype, pin_memory=True)
+    dq_in, dk_in, dv_in, dout = hq, hk, hv, hout
+    if heads is not None:
+        h0, h1 = heads
+        hq, hk, hv, hout = (t[:, :, h0:h1] for t in (hq, hk, hv, hout))
+        # the device-API caller holds its share in contiguous pinned buffers
+        dq_in, dk_in, dv_in, dout = (t.contiguous().pin_memory() for t in (hq, hk, hv, hout))
     h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
     d2h = hout.numel() * hout.element_size()
 
@@ -201,9 +231,9 @@ def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
         rdna4_sage.attention_host(hq, hk, hv, "NHD", out=hout, non_blocking=True)
 
     def device_api_step():
-        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (hq, hk, hv))
+        dq, dk, dv = (t.to(dev, non_blocking=True) for t in (dq_in, dk_in, dv_in))
         o = sageattention.sageattn(dq, dk, dv, tensor_layout="NHD")
-        hout.copy_(o, non_blocking=True)
+        dout.copy_(o, non_blocking=True)
 
     res = {}
     for name, fn in (("host", host_step), ("device_api", device_api_step)):
@@ -218,12 +248,18 @@ def run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks):
         torch.cuda.synchronize()
         res[name] = max_over_ranks(e0.elapsed_time(e1) / n)
     from rdna4_sage import _lib
-    B_, S_, H_, D_ = q.shape
+    B_, S_, H_, D_ = hq.shape
     hpc = _lib.lib().sage_host_heads_per_chunk(B_, H_, H_, S_, S_, D_, 0)
     return res["host"], res["device_api"], hpc, h2d, d2h
 
 
 HUNYUAN = (1, 24, 67576, 128)
+
+
+def _our_paths():
+    for pth in (PKG, ROOT):
+        if pth not in sys.path:
+            sys.path.insert(0, pth)
 
 
 def run_hunyuan_cp(args):
@@ -233,6 +269,7 @@ def run_hunyuan_cp(args):
 
     import torch.distributed as dist
 
+    _our_paths()
     import rdna4_sage
     from rdna4_sage import cp
 
@@ -285,6 +322,7 @@ def run_hunyuan_cp(args):
 
 
 def run_ours(args):
+    _our_paths()
     import rdna4_sage
     import sageattention
     from rdna4_sage import _lib
@@ -300,14 +338,18 @@ def run_ours(args):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    heads = args.heads
-    if args.strong and world > 1:
-        heads = args.heads // world + (1 if rank < args.heads % world else 0)
-    q, k, v = make_inputs(dev, h=heads, n=args.seq, seed=rank)
+    strong = world > 1 and not args.weak
+    # strong (default for N > 1): every rank holds the same call and computes its whole-GQA-group share of
+    # the heads (rdna4_sage.attention_shard); weak: every rank runs its own call
+    q, k, v = make_inputs(dev, h=args.heads, n=args.seq, seed=0 if strong else rank)
+    h0, h1 = rdna4_sage.shard_heads(args.heads, args.heads, world, rank) if strong else (0, args.heads)
+    heads = h1 - h0
     ops = ops_per_call(h=heads, n=args.seq)
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        if strong:
+            return rdna4_sage.attention_shard(q, k, v, "NHD", rank, world)
         return sageattention.sageattn(q, k, v, tensor_layout="NHD")
 
     assert rdna4_sage.is_available() and rdna4_sage._worth_it(q, k, "NHD")
@@ -339,16 +381,21 @@ def run_ours(args):
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     barrier()
     rdna4_sage._attention.check_status(dev)
-    total_ops = ops_per_call(h=args.heads, n=args.seq) if args.strong else ops * world
+    total_ops = ops_per_call(h=args.heads, n=args.seq) if strong else ops * world
     value = total_ops / (ms * 1e-3) / 1e12
 
     # ---- e2e: public API with pinned host buffers, copies inside every step
     ms_e2e, ms_e2e_dev, hpc, h2d, d2h = None, None, 0, 0, 0
     if not args.no_e2e:
-        ms_e2e, ms_e2e_dev, hpc, h2d, d2h = run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks)
+        ms_e2e, ms_e2e_dev, hpc, h2d, d2h = run_e2e(args, q, k, v, dev, stream, e0, e1, barrier, max_over_ranks,
+                                                    (h0, h1) if strong else None)
+        if strong:  # copies of all ranks together
+            h2d, d2h = h2d * world, d2h * world
 
-    # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream)
+    # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream), on this rank's heads
     L = _lib.lib()
+    if strong:
+        q, k, v = (t[:, :, h0:h1].contiguous() for t in (q, k, v))
     Bq, Sq, Hq, Dq = q.shape
     spad = (Sq + 31) // 32 * 32
     ws_bytes = L.sage_workspace_bytes(Bq, Hq, Hq, Sq, Sq, Dq)
@@ -435,7 +482,7 @@ def run_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak",
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": value / (ops_per_call() / (REF_WAN_MS * 1e-3) / 1e12),
             "vs_baseline_basis": "value / 139.1 TOPS (reference README.md:194: 158 ms/call for this shape on "
                                  "RX 9070 XT)",
@@ -443,10 +490,11 @@ def run_ours(args):
             "config": {"workload": WORKLOAD,
                        "arithmetic": "int8 QK^T (int32 accumulate), fp32 softmax, e4m3 PV (fp32 accumulate); "
                                      "bf16 in and out",
-                       "global_batch": 1 if args.strong else world, "seq_len": N,
+                       "global_batch": 1 if strong or world == 1 else world, "seq_len": N,
                        "heads_per_rank": heads,
-                       "parallelism": (f"heads split over {world} ranks" if args.strong else
-                                       f"dp{world}: one call's (batch, head) units per rank, no collective"),
+                       "parallelism": (f"one call's heads split over {world} ranks in whole GQA groups "
+                                       "(rdna4_sage.attention_shard), no collective" if strong else
+                                       f"dp{world}: every rank its own call, no collective"),
                        "l2": "inputs 1.0 GB per rank > 126 MB L2 (no flush needed)"},
             "clocks": clocks.summary(),
             "e2e": None if ms_e2e is None else
@@ -483,15 +531,17 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--strong", action="store_true", help="split the heads of one call across ranks")
+    ap.add_argument("--weak", action="store_true",
+                    help="N > 1: every rank runs its own whole call (default: one call's heads split over the ranks)")
     ap.add_argument("--workload", choices=["wan", "hunyuan"], default="wan",
                     help="wan: the metric's call; hunyuan: the >64K call with the sequence split over ranks")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-copy leg")
     ap.add_argument("--heads", type=int, default=H, help="heads per call (profiling: a smaller case)")
     ap.add_argument("--seq", type=int, default=N, help="tokens per call (profiling: a smaller case)")
+    ap.add_argument("--sample", action="store_true", help=argparse.SUPPRESS)  # reference arm as the CPU leg
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and not args.sample:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)

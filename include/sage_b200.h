@@ -151,6 +151,25 @@ int sage_attention_host(const void* q, const void* k, const void* v, int dtype, 
                         int64_t oss, int64_t osh, float* lse, int heads_per_chunk, void* workspace,
                         size_t workspace_bytes, int* status, void* stream);
 
+/* One call on tensors in HOST memory spread over several GPUs of the box (one process): the flattened
+ * (batch, kv head) units are split into n_devices contiguous shares, as equal as the unit count allows, and
+ * device d runs its share as sage_attention_host calls (whole GQA groups of query heads, one batch each) on
+ * streams[d] with workspaces[d] (device memory on devices[d], 256-byte aligned, workspace_bytes each, at least
+ * sage_host_multi_workspace_bytes) and statuses[d] (nullable array; NULL entries use the library's word of that
+ * device).  Units need no exchange (quantisation scales are per head), so there is no collective: each device
+ * copies in its inputs and copies its output heads (and LSE rows) back into `out` / `lse`.  The call returns
+ * once everything is enqueued; the result is complete when every streams[d] has finished.  The current device
+ * is left as it was.  The reference runs every call on one device (src/rdna4_sage/_attention.py:74-75); this
+ * replaces that for callers with several GPUs. */
+size_t sage_host_multi_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk,
+                                       int n_devices);
+int sage_attention_host_multi(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
+                              int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss,
+                              int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal,
+                              void* out, int64_t osb, int64_t oss, int64_t osh, float* lse, int heads_per_chunk,
+                              int n_devices, const int* devices, void* const* workspaces, size_t workspace_bytes,
+                              int* const* statuses, void* const* streams);
+
 /* Failure-path self test (no counterpart in the reference): enqueues a kernel whose single wait is on a
  * barrier that nothing completes, bounded by limit_ms (1..2000) instead of the pipeline's 2 s.  When the
  * work on `stream` is done, the status word (NULL = the library's own) holds SAGE_ERR_TIMEOUT, exactly as

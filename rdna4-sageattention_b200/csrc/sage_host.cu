@@ -301,4 +301,97 @@ int sage_attention_host(const void* q, const void* k, const void* v, int dtype, 
   return SAGE_OK;
 }
 
+// One device's share of a multi-device call: units u0 .. u1-1 of the flattened (batch, kv head) index,
+// cut at batch boundaries into pieces of one batch and a range of kv heads.
+struct Piece {
+  int b, g0, g1;
+};
+
+static std::vector<Piece> device_pieces(int B, int Hkv, int n_dev, int d) {
+  const int64_t units = (int64_t)B * Hkv;
+  const int64_t u0 = units * d / n_dev, u1 = units * (d + 1) / n_dev;
+  std::vector<Piece> out;
+  for (int64_t u = u0; u < u1;) {
+    const int b = (int)(u / Hkv), g0 = (int)(u % Hkv);
+    const int g1 = (int)std::min<int64_t>(Hkv, g0 + (u1 - u));
+    out.push_back({b, g0, g1});
+    u += g1 - g0;
+  }
+  return out;
+}
+
+size_t sage_host_multi_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk,
+                                       int n_devices) {
+  if (n_devices <= 0 || B <= 0 || Hkv <= 0 || H % Hkv != 0) return 0;
+  const int G = H / Hkv;
+  size_t need = 0;
+  for (int d = 0; d < n_devices; ++d)
+    for (const Piece& pc : device_pieces(B, Hkv, n_devices, d)) {
+      const int hkp = pc.g1 - pc.g0;
+      const int hpc = heads_per_chunk > 0 ? std::min(heads_per_chunk, hkp * G) : 0;
+      const size_t n = sage_host_workspace_bytes(1, hkp * G, hkp, Sq, Skv, D, hpc);
+      if (n == 0) return 0;
+      need = std::max(need, n);
+    }
+  return need;
+}
+
+int sage_attention_host_multi(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
+                              int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss,
+                              int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal,
+                              void* out, int64_t osb, int64_t oss, int64_t osh, float* lse, int heads_per_chunk,
+                              int n_devices, const int* devices, void* const* workspaces, size_t workspace_bytes,
+                              int* const* statuses, void* const* streams) {
+  NvtxRange nvtx("sage_attention_host_multi");
+  if (n_devices <= 0 || devices == nullptr || workspaces == nullptr || streams == nullptr) {
+    set_error("n_devices > 0 and device, workspace and stream arrays required");
+    return SAGE_ERR_INVALID;
+  }
+  if (B <= 0 || H <= 0 || Hkv <= 0 || H % Hkv != 0) {
+    set_error("sizes B=%d H=%d Hkv=%d (H a multiple of Hkv required)", B, H, Hkv);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  const size_t need = sage_host_multi_workspace_bytes(B, H, Hkv, Sq, Skv, D, heads_per_chunk, n_devices);
+  if (need == 0) {
+    set_error("unsupported sizes or heads_per_chunk %d", heads_per_chunk);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (workspace_bytes < need) {
+    set_error("workspace of %zu bytes per device required, got %zu", need, workspace_bytes);
+    return SAGE_ERR_INVALID;
+  }
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) {
+    set_error("cudaGetDevice failed");
+    return SAGE_ERR_LAUNCH;
+  }
+  const int G = H / Hkv;
+  const size_t es = 2;
+  int rc = SAGE_OK;
+  for (int d = 0; d < n_devices && rc == SAGE_OK; ++d) {
+    const cudaError_t e = cudaSetDevice(devices[d]);
+    if (e != cudaSuccess) {
+      set_error("cudaSetDevice(%d): %s", devices[d], cudaGetErrorString(e));
+      rc = SAGE_ERR_LAUNCH;
+      break;
+    }
+    // the device's pieces run one after the other on its stream, reusing its workspace
+    for (const Piece& pc : device_pieces(B, Hkv, n_devices, d)) {
+      const int hkp = pc.g1 - pc.g0, hp = hkp * G, h0 = pc.g0 * G;
+      const int hpc = heads_per_chunk > 0 ? std::min(heads_per_chunk, hp) : 0;
+      const char* qp = static_cast<const char*>(q) + ((int64_t)pc.b * qsb + (int64_t)h0 * qsh) * (int64_t)es;
+      const char* kp = static_cast<const char*>(k) + ((int64_t)pc.b * ksb + (int64_t)pc.g0 * ksh) * (int64_t)es;
+      const char* vp = static_cast<const char*>(v) + ((int64_t)pc.b * vsb + (int64_t)pc.g0 * vsh) * (int64_t)es;
+      char* op = static_cast<char*>(out) + ((int64_t)pc.b * osb + (int64_t)h0 * osh) * (int64_t)es;
+      float* lp = lse != nullptr ? lse + ((int64_t)pc.b * H + h0) * Sq : nullptr;
+      rc = sage_attention_host(qp, kp, vp, dtype, 1, hp, hkp, Sq, Skv, D, qsb, qss, qsh, ksb, kss, ksh, vsb, vss, vsh,
+                               sm_scale, causal, op, osb, oss, osh, lp, hpc, workspaces[d], workspace_bytes,
+                               statuses != nullptr ? statuses[d] : nullptr, streams[d]);
+      if (rc != SAGE_OK) break;
+    }
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
 }  // extern "C"

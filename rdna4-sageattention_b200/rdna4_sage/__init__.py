@@ -13,10 +13,12 @@ from torch.nn.attention.bias import causal_lower_right
 
 from . import ops
 from ._attention import (ARCHS, HEAD_DIMS, QuantizedKV, Unsupported, attention_host, attention_quantized_kv,
-                         check_supported, check_supported_varlen, device_arch, quantize_kv)
+                         attention_shard, check_supported, check_supported_varlen, device_arch, quantize_kv,
+                         shard_heads)
 
-__all__ = ["sageattn", "attention", "attention_varlen", "attention_host", "quantize_kv", "attention_quantized_kv",
-           "QuantizedKV", "is_available", "Unsupported", "ARCHS", "HEAD_DIMS"]
+__all__ = ["sageattn", "attention", "attention_varlen", "attention_host", "attention_shard", "shard_heads",
+           "quantize_kv", "attention_quantized_kv", "QuantizedKV", "is_available", "Unsupported", "ARCHS",
+           "HEAD_DIMS"]
 __version__ = "0.2.1+b200"
 
 # The C binding behind F.scaled_dot_product_attention. Apps replace F.scaled_dot_product_attention with

@@ -7,6 +7,7 @@ tcgen05 attention kernel, all on torch's current stream, buffers allocated by to
 """
 from __future__ import annotations
 
+import ctypes
 import math
 import os
 
@@ -291,16 +292,21 @@ def _bsh_host(t: torch.Tensor, layout: str):
 
 
 def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=False, device=None,
-                   heads_per_chunk=0, out=None, non_blocking=False):
+                   heads_per_chunk=0, out=None, non_blocking=False, devices=None):
     """attention() for q, k, v in host memory, with the copies to and from the GPU overlapped with the
     kernels (chunks of heads: copy in / attend / copy out on three streams, one C-ABI call).
 
     q, k, v: CPU tensors (pinned memory for the copies to overlap), shapes as for attention().  Returns
     the result in q's layout, a view of a pinned CPU (B, Sq, H, D) buffer (or of `out`, a CPU tensor of
     that shape and dtype), and with return_lse also the (B, H, Sq) fp32 LSE on the CPU.  `device`: the GPU to run on
-    (default: the current one).  With non_blocking=True the call returns once the work is enqueued on
-    torch's current stream of that device; the results are valid after that stream synchronises.
+    (default: the current one).  `devices`: a list of GPUs to spread the call over instead (its
+    (batch, kv head) units split evenly, each GPU running its share's chunk pipeline; no collective).
+    With non_blocking=True the call returns once the work is enqueued on torch's current stream of each
+    GPU; the results are valid after those streams synchronise.
     """
+    if devices is not None:
+        return _attention_host_multi(q, k, v, layout, sm_scale, is_causal, return_lse, list(devices),
+                                     heads_per_chunk, out, non_blocking)
     if layout not in ("HND", "NHD"):
         raise Unsupported(f"layout {layout!r}")
     if q.is_cuda or k.is_cuda or v.is_cuda:
@@ -344,6 +350,96 @@ def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return
             check_status(dev)
     res = out.transpose(1, 2) if layout == "HND" else out
     return (res, lse) if return_lse else res
+
+
+_MULTI_WS = {}  # device index -> cached workspace of the multi-GPU host calls
+
+
+def _attention_host_multi(q, k, v, layout, sm_scale, is_causal, return_lse, devices, heads_per_chunk, out,
+                          non_blocking):
+    """attention_host over several GPUs: one sage_attention_host_multi call (C ABI)."""
+    if layout not in ("HND", "NHD"):
+        raise Unsupported(f"layout {layout!r}")
+    if q.is_cuda or k.is_cuda or v.is_cuda:
+        raise Unsupported("attention_host takes host tensors; use attention() for GPU tensors")
+    _check_shapes(q, k, v, layout, is_causal)
+    devs = [torch.device("cuda", int(d) if not isinstance(d, torch.device) else d.index) for d in devices]
+    if not devs or len({d.index for d in devs}) != len(devs):
+        raise ValueError("devices must be a non-empty list of distinct GPUs")
+    for d in devs:
+        _check_arch(d)
+    L = _lib.lib()
+    if layout == "HND":
+        B, H, Sq, D = q.shape
+        Hkv, Skv = k.shape[1], k.shape[2]
+    else:
+        B, Sq, H, D = q.shape
+        Skv, Hkv = k.shape[1], k.shape[2]
+    q, sq_ = _bsh_host(q, layout)
+    k, sk_ = _bsh_host(k, layout)
+    v, sv_ = _bsh_host(v, layout)
+    if out is None:
+        out = torch.empty((B, Sq, H, D), dtype=q.dtype, pin_memory=True)
+    elif out.is_cuda or out.shape != (B, Sq, H, D) or out.dtype != q.dtype or out.stride(-1) != 1:
+        raise ValueError("out must be a CPU tensor of shape (B, Sq, H, D) in q's dtype, channel axis contiguous")
+    lse = torch.empty((B, H, Sq), dtype=torch.float32, pin_memory=True) if return_lse else None
+    n = len(devs)
+    ws_bytes = L.sage_host_multi_workspace_bytes(B, H, Hkv, Sq, Skv, D, int(heads_per_chunk), n)
+    if ws_bytes == 0:
+        raise Unsupported(f"heads_per_chunk {heads_per_chunk} or sizes not supported over {n} GPUs")
+    ws, streams, statuses = [], [], []
+    for d in devs:
+        w = _MULTI_WS.get(d.index)
+        if w is None or w.numel() < ws_bytes:
+            w = torch.empty(ws_bytes, device=d, dtype=torch.uint8)
+            _MULTI_WS[d.index] = w
+        ws.append(w)
+        streams.append(torch.cuda.current_stream(d))
+        statuses.append(status_word(d))
+    arr = lambda ctype, vals: (ctype * n)(*vals)  # noqa: E731
+    rc = L.sage_attention_host_multi(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPES[q.dtype], B, H, Hkv, Sq, Skv, D, *sq_, *sk_, *sv_,
+        float(sm_scale or 0.0), int(bool(is_causal)), out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+        lse.data_ptr() if lse is not None else None, int(heads_per_chunk), n,
+        arr(ctypes.c_int, [d.index for d in devs]), arr(ctypes.c_void_p, [w.data_ptr() for w in ws]), ws_bytes,
+        arr(ctypes.c_void_p, [t.data_ptr() for t in statuses]), arr(ctypes.c_void_p, [st.cuda_stream for st in streams]))
+    _lib.check(rc, "sage_attention_host_multi")
+    for w, st in zip(ws, streams):
+        w.record_stream(st)
+    if not non_blocking:
+        for st in streams:
+            st.synchronize()
+    if _CHECK:
+        for d in devs:
+            check_status(d)
+    res = out.transpose(1, 2) if layout == "HND" else out
+    return (res, lse) if return_lse else res
+
+
+def shard_heads(H, Hkv, world, rank):
+    """Query-head range [h0, h1) of `rank` when one call's heads are split over `world` GPUs in whole GQA groups
+    (kv heads dealt as evenly as possible; ranks past Hkv get an empty range)."""
+    if world <= 0 or not 0 <= rank < world or Hkv <= 0 or H % Hkv:
+        raise ValueError(f"shard_heads(H={H}, Hkv={Hkv}, world={world}, rank={rank})")
+    g = H // Hkv
+    return Hkv * rank // world * g, Hkv * (rank + 1) // world * g
+
+
+def attention_shard(q, k, v, layout="HND", rank=0, world=1, sm_scale=None, is_causal=False, return_lse=False):
+    """This rank's share of one attention call split by heads over `world` GPUs (one process per GPU): the
+    full-call q, k, v on this rank's GPU; computes heads shard_heads(H, Hkv, world, rank) on strided views
+    (no copies, no collective: the units are independent) and returns their output in the input layout
+    (heads axis of size h1 - h0), plus the (B, h1 - h0, Sq) LSE with return_lse."""
+    H = q.shape[1] if layout == "HND" else q.shape[2]
+    Hkv = k.shape[1] if layout == "HND" else k.shape[2]
+    h0, h1 = shard_heads(H, Hkv, world, rank)
+    g = H // Hkv
+    ax = 1 if layout == "HND" else 2
+    qs_, ks_, vs_ = q.narrow(ax, h0, h1 - h0), k.narrow(ax, h0 // g, (h1 - h0) // g), v.narrow(ax, h0 // g, (h1 - h0) // g)
+    res = attention(qs_, ks_, vs_, layout, sm_scale, is_causal, return_lse)
+    o, lse = res if return_lse else (res, None)
+    o = o.transpose(1, 2) if layout == "HND" else o
+    return (o, lse) if return_lse else o
 
 
 def sm_fold(sm_scale, head_dim):

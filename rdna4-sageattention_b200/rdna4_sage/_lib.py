@@ -61,6 +61,10 @@ SIGNATURES = {
     "sage_attention_host": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,
                                    _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,
                                    _c_i64, _c_i64, _c_i64, _c_p, _c_i, _c_p, _c_sz, _c_p, _c_p]),
+    "sage_host_multi_workspace_bytes": (_c_sz, [_c_i] * 8),
+    "sage_attention_host_multi": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,
+                                         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,
+                                         _c_i64, _c_i64, _c_i64, _c_p, _c_i, _c_i, _c_p, _c_p, _c_sz, _c_p, _c_p]),
     "sage_selftest_wait_timeout": (_c_i, [_c_p, _c_i, _c_p]),
     "sage_selftest_counter_timeout": (_c_i, [_c_p, _c_p, _c_i, _c_p]),
     "sage_status_sync": (_c_i, [_c_p, _c_p]),

@@ -100,3 +100,17 @@ def test_varlen_cpu_loops_like_reference():
         ref = torch._C._nn.scaled_dot_product_attention(q[None, a:b].transpose(1, 2), k[None, a:b].transpose(1, 2),
                                                        v[None, a:b].transpose(1, 2)).transpose(1, 2)[0]
         assert torch.equal(out[a:b], ref)
+
+
+def test_shard_heads_covers_every_head_once_in_whole_groups():
+    import rdna4_sage
+    for H, Hkv, world in [(40, 40, 8), (40, 40, 3), (32, 8, 8), (32, 8, 3), (24, 8, 16), (16, 4, 1)]:
+        seen = []
+        for rank in range(world):
+            h0, h1 = rdna4_sage.shard_heads(H, Hkv, world, rank)
+            assert h0 % (H // Hkv) == 0 and h1 % (H // Hkv) == 0 and 0 <= h0 <= h1 <= H
+            seen.extend(range(h0, h1))
+        assert seen == list(range(H)), (H, Hkv, world)
+        sizes = [rdna4_sage.shard_heads(H, Hkv, world, r) for r in range(world)]
+        counts = [(b - a) // (H // Hkv) for a, b in sizes]
+        assert max(counts) - min(counts) <= 1

@@ -1,10 +1,11 @@
-"""SageAttention-style int8 QK / fp8 PV attention for NVIDIA B200 (sm_100a).
+"""int8 QK^T / fp8 PV SageAttention kernels for NVIDIA B200 (sm_100a), loaded from libsage_b200.so.
 
-Hand-written tcgen05 / TMA CUDA kernels behind a C-ABI library (libsage_b200.so), launched on torch's
-current stream.  Same public surface as the reference package (src/rdna4_sage/__init__.py:17):
+Public names as in the reference package (src/rdna4_sage/__init__.py:17): ``sageattn``, ``attention``,
+``is_available``, ``Unsupported``, ``ARCHS``, ``HEAD_DIMS``; plus the B200 additions (varlen, host-memory and
+multi-GPU entries, the quantised K/V cache).  Example::
 
     import rdna4_sage
-    out = rdna4_sage.sageattn(q, k, v, tensor_layout="HND")   # drop-in for sageattention.sageattn
+    o = rdna4_sage.sageattn(q, k, v, tensor_layout="HND")
 """
 import os
 
@@ -21,28 +22,31 @@ __all__ = ["sageattn", "attention", "attention_varlen", "attention_host", "atten
            "HEAD_DIMS"]
 __version__ = "0.2.1+b200"
 
-# The C binding behind F.scaled_dot_product_attention. Apps replace F.scaled_dot_product_attention with
-# sageattn, so falling back through F would call back into sageattn forever (reference __init__.py:20-22).
+# SDPA through its C binding: applications often replace torch.nn.functional.scaled_dot_product_attention
+# by sageattn, and routing back through the Python name would then re-enter sageattn.
 _torch_sdpa = torch._C._nn.scaled_dot_product_attention
 
-# Calls below these sizes run torch SDPA: the fixed quantization pass costs more than int8 attention saves.
-MIN_WORK = int(os.environ.get("RDNA4_SAGE_MIN_WORK", 64 * 2**20))  # batch * heads * q_len * kv_len
-MIN_KV = int(os.environ.get("RDNA4_SAGE_MIN_KV", 1024))           # short text contexts stay on SDPA
+# Routing thresholds (same names, defaults and environment overrides as the reference).  A call goes to the
+# quantised kernels only when kv_len >= MIN_KV and B * H * q_len * kv_len (halved for causal) >= MIN_WORK;
+# smaller calls are dominated by the fixed cost of the quantisation pass and run SDPA.
+MIN_WORK = int(os.environ.get("RDNA4_SAGE_MIN_WORK", 64 * 2**20))
+MIN_KV = int(os.environ.get("RDNA4_SAGE_MIN_KV", 1024))
 
 
 def is_available(device=None) -> bool:
-    """True when the current (or given) GPU is sm_100 (B200 / GB200), the only GPUs the kernels are built for."""
-    if not torch.cuda.is_available() or torch.version.hip is not None:
+    """Whether `device` (default: the current CUDA device) is a GPU the kernels are compiled for (sm_100)."""
+    if torch.version.hip is not None or not torch.cuda.is_available():
         return False
-    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
-    return device_arch(dev) in ARCHS
+    index = torch.cuda.current_device() if device is None else (torch.device(device).index or 0)
+    return device_arch(torch.device("cuda", index)) in ARCHS
 
 
 def attention(q, k, v, tensor_layout="HND", sm_scale=None, is_causal=False):
-    """Run the int8/fp8 kernel; raises Unsupported if it cannot. Output in the input layout and dtype.
-    Causal attention needs q_len == kv_len."""
-    out = ops.attention(q, k, v, tensor_layout, float(sm_scale or 0.0), bool(is_causal))
-    return out.transpose(1, 2) if tensor_layout == "HND" else out
+    """The quantised attention kernels on q, k, v (no routing): the result in the input layout and dtype.
+    Raises Unsupported for inputs the kernels do not take.  Causal calls need q_len == kv_len."""
+    res = ops.attention(q, k, v, tensor_layout, float(sm_scale or 0.0), bool(is_causal))
+    # the op returns (B, q_len, H, D); HND callers get the transposed view
+    return res if tensor_layout == "NHD" else res.transpose(1, 2)
 
 
 def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, sm_scale=None,
@@ -54,44 +58,49 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seql
 
 
 def _sdpa(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask):
+    """torch SDPA in HND with SageAttention's conventions: causal masks aligned to the bottom right (they
+    matter when q_len != kv_len or when combined with a caller's mask) and GQA heads shared by groups."""
     if tensor_layout == "NHD":
-        q, k, v = (t.transpose(1, 2) for t in (q, k, v))
-    gqa = q.shape[1] != k.shape[1]
-    Sq, Skv = q.shape[2], k.shape[2]
-    if is_causal and (Sq != Skv or attn_mask is not None):
-        # SageAttention / FlashAttention semantics: bottom-right aligned causal mask
-        causal = causal_lower_right(Sq, Skv)._materialize(q.device)
+        q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    q_len, kv_len = q.shape[2], k.shape[2]
+    needs_explicit = is_causal and (attn_mask is not None or q_len != kv_len)
+    if needs_explicit:
+        keep = causal_lower_right(q_len, kv_len)._materialize(q.device)
         if attn_mask is None:
-            attn_mask = causal
+            attn_mask = keep
+        elif attn_mask.dtype == torch.bool:
+            attn_mask = attn_mask & keep
         else:
-            attn_mask = (attn_mask.masked_fill(~causal, float("-inf")) if attn_mask.dtype != torch.bool
-                         else attn_mask & causal)
+            attn_mask = attn_mask.masked_fill(~keep, float("-inf"))
         is_causal = False
-    out = _torch_sdpa(q, k, v, attn_mask=attn_mask, is_causal=is_causal, scale=sm_scale, enable_gqa=gqa)
-    return out.transpose(1, 2) if tensor_layout == "NHD" else out
+    o = _torch_sdpa(q, k, v, attn_mask=attn_mask, is_causal=is_causal, scale=sm_scale,
+                    enable_gqa=q.shape[1] != k.shape[1])
+    return o.transpose(1, 2) if tensor_layout == "NHD" else o
 
 
 def _worth_it(q, k, tensor_layout, is_causal=False):
-    if tensor_layout == "HND":
-        B, H, Sq, _ = q.shape
-        Skv = k.shape[2]
-    else:
-        B, Sq, H, _ = q.shape
-        Skv = k.shape[1]
-    work = B * H * Sq * Skv // (2 if is_causal else 1)
-    return Skv >= MIN_KV and work >= MIN_WORK
+    """The size rule: enough keys and enough (query, key) pairs for the quantisation pass to pay off."""
+    heads_ax, seq_ax = (1, 2) if tensor_layout == "HND" else (2, 1)
+    batch, heads, q_len, kv_len = q.shape[0], q.shape[heads_ax], q.shape[seq_ax], k.shape[seq_ax]
+    pairs = batch * heads * q_len * kv_len
+    if is_causal:
+        pairs //= 2
+    return kv_len >= MIN_KV and pairs >= MIN_WORK
 
 
 def sageattn(q, k, v, tensor_layout="HND", is_causal=False, sm_scale=None, attn_mask=None, return_lse=False, **kwargs):
-    """Drop-in for sageattention.sageattn. Uses the B200 kernel when it applies and pays off, torch SDPA otherwise
-    (masks, causal with q_len != kv_len, LSE, unsupported shapes or GPUs, small problems). Causal attention is
-    bottom-right aligned as in SageAttention / FlashAttention. Extra SageAttention kwargs are ignored."""
+    """Drop-in for sageattention.sageattn.  The B200 kernels take the call when they support it and it is large
+    enough (_worth_it); masks, unsupported shapes, dtypes or GPUs and small calls run torch SDPA.  Causal masks
+    are bottom-right aligned, as in SageAttention and FlashAttention.  Other SageAttention keyword arguments
+    are accepted and ignored."""
     if return_lse:
         raise NotImplementedError("rdna4_sage: return_lse is not supported")
-    if attn_mask is not None or not _worth_it(q, k, tensor_layout, is_causal):
-        return _sdpa(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask)
-    try:
-        check_supported(q, k, v, tensor_layout, is_causal)
-    except Unsupported:
+    use_kernel = attn_mask is None and _worth_it(q, k, tensor_layout, is_causal)
+    if use_kernel:
+        try:
+            check_supported(q, k, v, tensor_layout, is_causal)
+        except Unsupported:
+            use_kernel = False
+    if not use_kernel:
         return _sdpa(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask)
     return attention(q, k, v, tensor_layout, sm_scale, is_causal)

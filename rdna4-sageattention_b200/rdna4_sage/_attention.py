@@ -96,9 +96,57 @@ def status_word(device: torch.device) -> torch.Tensor:
     return w
 
 
+# Device-side errors (a bounded wait that expired, inconsistent varlen tables) end up in the device's status
+# word.  Each call copies that word to pinned host memory after its kernels (asynchronously, on the same
+# stream) and records an event; the next call on the device reads the copy once the event has completed and
+# raises RuntimeError if it holds an error.  No call waits for the GPU for this.
+_watch: dict[int, tuple[torch.cuda.Event, torch.Tensor]] = {}
+
+
+def _raise_pending(device: torch.device) -> None:
+    """Raise RuntimeError if work that completed on `device` since the last check reported an error."""
+    w = _watch.get(device.index)
+    if w is None or not w[0].query():
+        return
+    code = int(w[1][0])
+    if code != 0:
+        del _watch[device.index]
+        status_word(device).zero_()
+        raise RuntimeError(f"rdna4_sage: an earlier kernel on cuda:{device.index} failed: "
+                           f"{_lib.STATUS_NAMES.get(code, code)} (see check_status)")
+
+
+def _watch_status(device: torch.device) -> None:
+    """Queue the copy of `device`'s status word behind the work just enqueued (skipped while capturing a
+    CUDA graph, where it would be replayed with stale buffers)."""
+    if torch.cuda.is_current_stream_capturing():
+        return
+    w = _watch.get(device.index)
+    if w is None:
+        w = (torch.cuda.Event(), torch.zeros(1, dtype=torch.int32, pin_memory=True))
+    else:
+        w[0].synchronize()  # the previous copy into the buffer (normally long done)
+    with torch.cuda.device(device):
+        w[1].copy_(status_word(device), non_blocking=True)
+        w[0].record(torch.cuda.current_stream(device))
+    _watch[device.index] = w
+
+
+def selftest_wait_timeout(limit_ms: int, device: torch.device | None = None) -> None:
+    """Run the library's bounded-wait self test on `device` against its status word (as after a stalled
+    pipeline stage): a later call on the device raises RuntimeError once the test kernel has finished."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.lib().sage_selftest_wait_timeout(status_word(dev).data_ptr(), int(limit_ms),
+                                                         torch.cuda.current_stream(dev).cuda_stream),
+                   "sage_selftest_wait_timeout")
+    _watch_status(dev)
+
+
 def check_status(device: torch.device | None = None) -> None:
     """Synchronise and raise RuntimeError if a kernel on `device` reported an error since the last check."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    _watch.pop(dev.index, None)  # this read covers what the watched copy would report
     w = status_word(dev)
     with torch.cuda.device(dev):
         rc = _lib.lib().sage_status_sync(w.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
@@ -112,6 +160,7 @@ def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=
     check_supported(q, k, v, layout, is_causal)
     L = _lib.lib()
     dev = q.device
+    _raise_pending(dev)
     if layout == "HND":
         B, H, Sq, D = q.shape
         Hkv, Skv = k.shape[1], k.shape[2]
@@ -131,6 +180,7 @@ def attention(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=
                           out.stride(0), out.stride(1), out.stride(2), lse.data_ptr() if lse is not None else None,
                           ws.data_ptr(), ws_bytes, status_word(dev).data_ptr(), stream)
     _lib.check(rc, "sage_attention")
+    _watch_status(dev)
     if _CHECK:
         check_status(dev)
     return (out, lse) if return_lse else out
@@ -200,6 +250,7 @@ def attention_quantized_kv(q, kv, tensor_layout="HND", sm_scale=None, is_causal=
         raise Unsupported("causal attention needs q_len == kv_len")
     L = _lib.lib()
     dev = q.device
+    _raise_pending(dev)
     q, sq_ = _bsh(q, tensor_layout)
     dk = L.sage_qk_row_bytes(D)
     q8 = torch.empty((B, H, Sq, dk), device=dev, dtype=torch.int8)
@@ -214,6 +265,7 @@ def attention_quantized_kv(q, kv, tensor_layout="HND", sm_scale=None, is_causal=
                                int(bool(is_causal)), out.stride(0), out.stride(1), out.stride(2),
                                lse.data_ptr() if lse is not None else None, status_word(dev).data_ptr(), stream),
                "sage_attn_fwd")
+    _watch_status(dev)
     if _CHECK:
         check_status(dev)
     return (out, lse) if return_lse else out
@@ -260,6 +312,7 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seql
     check_supported_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k)
     L = _lib.lib()
     dev = q.device
+    _raise_pending(dev)
     total_q, H, D = q.shape
     total_k, Hkv = k.shape[0], k.shape[1]
     nseq = cu_seqlens_q.numel() - 1
@@ -278,6 +331,7 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seql
                                  out.stride(0), out.stride(1), lse.data_ptr() if lse is not None else None,
                                  ws.data_ptr(), ws_bytes, status_word(dev).data_ptr(), stream)
     _lib.check(rc, "sage_attention_varlen")
+    _watch_status(dev)
     if _CHECK:
         check_status(dev)
     return (out, lse) if return_lse else out
@@ -332,6 +386,7 @@ def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return
     hpc = L.sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, int(heads_per_chunk))
     if hpc == 0:
         raise Unsupported(f"heads_per_chunk {heads_per_chunk} (a multiple of H / Hkv = {H // Hkv} required)")
+    _raise_pending(dev)
     with torch.cuda.device(dev):
         ws_bytes = L.sage_host_workspace_bytes(B, H, Hkv, Sq, Skv, D, hpc)
         ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
@@ -342,6 +397,7 @@ def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return
                                    lse.data_ptr() if lse is not None else None, hpc, ws.data_ptr(), ws_bytes,
                                    status_word(dev).data_ptr(), stream.cuda_stream)
         _lib.check(rc, "sage_attention_host")
+        _watch_status(dev)
         # the workspace goes back to torch's pool only after the stream has finished with it
         ws.record_stream(stream)
         if not non_blocking:
@@ -368,6 +424,7 @@ def _attention_host_multi(q, k, v, layout, sm_scale, is_causal, return_lse, devi
         raise ValueError("devices must be a non-empty list of distinct GPUs")
     for d in devs:
         _check_arch(d)
+        _raise_pending(d)
     L = _lib.lib()
     if layout == "HND":
         B, H, Sq, D = q.shape
@@ -404,8 +461,9 @@ def _attention_host_multi(q, k, v, layout, sm_scale, is_causal, return_lse, devi
         arr(ctypes.c_int, [d.index for d in devs]), arr(ctypes.c_void_p, [w.data_ptr() for w in ws]), ws_bytes,
         arr(ctypes.c_void_p, [t.data_ptr() for t in statuses]), arr(ctypes.c_void_p, [st.cuda_stream for st in streams]))
     _lib.check(rc, "sage_attention_host_multi")
-    for w, st in zip(ws, streams):
+    for d, w, st in zip(devs, ws, streams):
         w.record_stream(st)
+        _watch_status(d)
     if not non_blocking:
         for st in streams:
             st.synchronize()

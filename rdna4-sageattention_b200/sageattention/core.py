@@ -20,34 +20,41 @@ import rdna4_sage
 from rdna4_sage import ops as _ops
 
 
-def _to_hnd(t, tensor_layout):
-    if tensor_layout not in ("HND", "NHD"):
-        raise ValueError(f"tensor_layout must be 'HND' or 'NHD', got {tensor_layout!r}")
-    return t if tensor_layout == "HND" else t.transpose(1, 2)
+def _hnd(t, tensor_layout):
+    """(B, H, L, D) view of a tensor given in `tensor_layout` ("HND" or "NHD")."""
+    if tensor_layout == "HND":
+        return t
+    if tensor_layout == "NHD":
+        return t.transpose(1, 2)
+    raise ValueError(f"tensor_layout must be 'HND' or 'NHD', got {tensor_layout!r}")
+
+
+_LSE_SCORES_PER_MATMUL = 64 * 2**20  # fp32 logits formed at a time: 256 MB
 
 
 def _lse(q, k, tensor_layout, is_causal, sm_scale):
-    """logsumexp over keys of Q K^T * sm_scale, shape [B, H, q_len], fp32 (SageAttention's return_lse output).
-    Computed in chunks with torch, as the reference shim does (core.py:23-44)."""
-    q, k = _to_hnd(q, tensor_layout), _to_hnd(k, tensor_layout)
-    B, H, Sq, D = q.shape
-    Skv = k.shape[2]
-    if k.shape[1] != H:
-        k = k.repeat_interleave(H // k.shape[1], dim=1)
+    """Log-sum-exp over keys of the scaled logits, (B, H, q_len) fp32, computed in torch: what the reference
+    returns for return_lse (src/sageattention/core.py:23-44) and what calls routed to SDPA return here.
+    One (batch, head) at a time, its query rows in chunks whose fp32 logits stay under 256 MB; GQA heads use
+    their group's kv head; causal masks are bottom-right aligned."""
+    qh, kh = _hnd(q, tensor_layout), _hnd(k, tensor_layout)
+    B, H, q_len, D = qh.shape
+    kv_len = kh.shape[2]
+    group = H // kh.shape[1]
     scale = D ** -0.5 if sm_scale is None else sm_scale
-    out = torch.empty((B, H, Sq), device=q.device, dtype=torch.float32)
-    rows = max(1, (64 * 2**20) // max(1, Skv))  # ~256 MB of fp32 scores per chunk and head
-    cols = torch.arange(Skv, device=q.device)
+    step = max(1, _LSE_SCORES_PER_MATMUL // max(1, kv_len))
+    key_pos = torch.arange(kv_len, device=q.device)
+    res = torch.empty((B, H, q_len), device=q.device, dtype=torch.float32)
     for b in range(B):
         for h in range(H):
-            kf = k[b, h].float()
-            for s in range(0, Sq, rows):
-                sc = q[b, h, s:s + rows].float() @ kf.T * scale
-                if is_causal:  # bottom-right aligned, as the kernels
-                    r = torch.arange(s, s + sc.shape[0], device=q.device)[:, None]
-                    sc.masked_fill_(cols[None, :] > r + (Skv - Sq), float("-inf"))
-                out[b, h, s:s + rows] = torch.logsumexp(sc, dim=-1)
-    return out
+            keys_t = kh[b, h // group].float().T
+            for r0 in range(0, q_len, step):
+                logits = qh[b, h, r0:r0 + step].float() @ keys_t * scale
+                if is_causal:
+                    row_pos = torch.arange(r0, r0 + logits.shape[0], device=q.device)
+                    logits.masked_fill_(key_pos[None, :] > row_pos[:, None] + (kv_len - q_len), float("-inf"))
+                res[b, h, r0:r0 + step] = torch.logsumexp(logits, dim=-1)
+    return res
 
 
 def _kernel_lse_call(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask):
@@ -113,21 +120,22 @@ def sageattn_varlen(
         else:
             return rdna4_sage.attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k,
                                                sm_scale=sm_scale, is_causal=is_causal)
-    cq = cu_seqlens_q.tolist()
-    ck = cu_seqlens_k.tolist()
+    # each sequence as its own call (reads the offsets back to the host, as the reference's loop does)
+    bounds_q, bounds_k = cu_seqlens_q.tolist(), cu_seqlens_k.tolist()
     out = torch.empty_like(q)
-    for i in range(len(cq) - 1):
-        if cq[i + 1] == cq[i]:
-            continue
-        o = sageattn(q[None, cq[i]:cq[i + 1]], k[None, ck[i]:ck[i + 1]], v[None, ck[i]:ck[i + 1]], tensor_layout="NHD",
-                     is_causal=is_causal, sm_scale=sm_scale)
-        out[cq[i]:cq[i + 1]] = o[0]
+    for (q0, q1), (k0, k1) in zip(zip(bounds_q, bounds_q[1:]), zip(bounds_k, bounds_k[1:])):
+        if q1 > q0:
+            o = sageattn(q[q0:q1].unsqueeze(0), k[k0:k1].unsqueeze(0), v[k0:k1].unsqueeze(0), tensor_layout="NHD",
+                         is_causal=is_causal, sm_scale=sm_scale)
+            out[q0:q1] = o[0]
     return out
 
 
 def _variant(q, k, v, tensor_layout="HND", is_causal=False, sm_scale=None, return_lse=False, **kwargs):
-    return sageattn(q, k, v, tensor_layout=tensor_layout, is_causal=is_causal, sm_scale=sm_scale, return_lse=return_lse,
-                    attn_mask=kwargs.get("attn_mask"))
+    """The SageAttention kernel-choice variants below all run sageattn: only the mask among their extra
+    arguments changes the result."""
+    return sageattn(q, k, v, tensor_layout=tensor_layout, is_causal=is_causal, sm_scale=sm_scale,
+                    return_lse=return_lse, attn_mask=kwargs.get("attn_mask"))
 
 
 def sageattn_qk_int8_pv_fp16_triton(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, tensor_layout: str = "HND",

@@ -76,7 +76,7 @@ def test_routing_on_cpu_and_errors():
     with pytest.raises(rdna4_sage.Unsupported):
         rdna4_sage.check_supported(q, q, q, "BHSD")
     with pytest.raises(ValueError):
-        sageattention.core._to_hnd(q, "XYZ")
+        sageattention.core._hnd(q, "XYZ")
     assert not rdna4_sage.is_available() or torch.cuda.is_available()
 
 

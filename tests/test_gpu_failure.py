@@ -52,3 +52,24 @@ def test_expired_counter_wait_raises_abort_flag():
     assert words.tolist() == [0, 1]
     assert L.sage_status_sync(word.data_ptr(), stream) == _lib.SAGE_ERR_TIMEOUT
     assert L.sage_selftest_counter_timeout(None, None, 100, None) == _lib.SAGE_ERR_INVALID
+
+
+def test_device_error_raises_at_a_later_call_without_opting_in():
+    """A kernel-side error surfaces as RuntimeError at the next call on the device (the reference raises its
+    launch errors, src/rdna4_sage/_hip.py:47-49), with no per-call synchronisation and no RDNA4_SAGE_CHECK."""
+    dev = torch.device("cuda", 0)
+    _attention.check_status(dev)                      # start clean
+    q = torch.randn(1, 24, 4096, 128, device=dev, dtype=torch.bfloat16)   # a call sageattn routes to the kernel
+    assert rdna4_sage._worth_it(q, q, "HND")
+    rdna4_sage.attention(q, q, q, "HND")              # a normal call first: nothing pending
+    _attention.selftest_wait_timeout(20, dev)         # a pipeline wait that expires
+    torch.cuda.synchronize()                          # (the test only makes the order deterministic)
+    with pytest.raises(RuntimeError, match="timeout"):
+        import sageattention
+        sageattention.sageattn(q, q, q, tensor_layout="HND")
+    # the error was reported once and cleared: the next calls run normally
+    out = rdna4_sage.attention(q, q, q, "HND")
+    torch.cuda.synchronize()
+    rdna4_sage.attention(q, q, q, "HND")
+    _attention.check_status(dev)
+    assert torch.isfinite(out).all()

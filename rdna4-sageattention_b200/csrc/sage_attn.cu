@@ -53,6 +53,7 @@ struct AttnParams {
   int64_t o_sb, o_ss, o_sh;
   int B, H, Hkv, Sq, Skv, nkb;
   int q_groups;  // number of QT*128-row query groups per (batch, head)
+  int unit0;     // non-causal dense launches: (plane, query group) index of this launch's first CTA
   float sm_log2e;
   int out_f16;
   // packed variable-length batches (cu_q == nullptr: dense): B counts sequences, Sq / Skv are unused
@@ -64,9 +65,10 @@ struct AttnParams {
   int64_t pad_total;
 };
 
-template <int D>
+// SINGLE: one 128-row Q tile per CTA whatever D (the launch that finishes a call's last, partial wave)
+template <int D, bool SINGLE = false>
 struct AttnCfg {
-  static constexpr int QT = D == 64 ? 4 : (D <= 128 ? 2 : 1);         // 128-row Q tiles per CTA
+  static constexpr int QT = SINGLE ? 1 : (D == 64 ? 4 : (D <= 128 ? 2 : 1));  // 128-row Q tiles per CTA
   static constexpr int DK = D == 64 ? 64 : (D == 256 ? 256 : 128);    // int8 bytes per Q/K row
   static constexpr int SW = DK >= 128 ? 128 : 64;                     // swizzle width of a Q/K box
   static constexpr int BM = 128;
@@ -282,7 +284,7 @@ __device__ __noinline__ void rescale_o(uint32_t taddr, float f) {
 // until the softmax warps have scaled their rows of O; then the rest, committed to o_done.  Block 0 has
 // been issued.  Returns the number of splits, or -1 if a wait gave up.
 template <int D, int NB>
-__device__ __noinline__ int pv_split(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_smem, uint32_t msk,
+__device__ __forceinline__ int pv_split(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_smem, uint32_t msk,
                                      uint64_t* o_part, uint64_t* o_fix, uint64_t* o_done, int nsplit,
                                      const WaitCtx wc) {
   constexpr uint32_t kIdescPV = idesc_e4m3(128, D);
@@ -300,11 +302,11 @@ __device__ __noinline__ int pv_split(uint32_t o_tmem, uint32_t p_tmem, uint32_t 
   return n;
 }
 
-template <int D, bool CAUSAL>
-__global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
+template <int D, bool CAUSAL, bool SINGLE>
+__global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
-  using C = AttnCfg<D>;
+  using C = AttnCfg<D, SINGLE>;
   constexpr int QT = C::QT;
   constexpr int NST = C::NST;
   constexpr int NB = C::NB;
@@ -336,8 +338,9 @@ __global__ void __launch_bounds__(AttnCfg<D>::THREADS, 1)
   // first across all (batch, head) planes (group-major), so that the last wave holds the shortest tiles;
   // measured faster than longest-first within each plane also when the planes' K / V exceed L2.
   const int n_bh = (int)(gridDim.x / (unsigned)p.q_groups);
-  const int grp = CAUSAL ? p.q_groups - 1 - (int)blockIdx.x / n_bh : (int)blockIdx.x % p.q_groups;
-  const int bh = CAUSAL ? (int)blockIdx.x % n_bh : (int)blockIdx.x / p.q_groups;
+  const int unit = p.unit0 + (int)blockIdx.x;
+  const int grp = CAUSAL ? p.q_groups - 1 - (int)blockIdx.x / n_bh : unit % p.q_groups;
+  const int bh = CAUSAL ? (int)blockIdx.x % n_bh : unit / p.q_groups;
   const int b = bh / p.H;
   const int h = bh - b * p.H;
   const int hkv = h / (p.H / p.Hkv);
@@ -796,6 +799,72 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
   return true;
 }
 
+// One launch of sage_attn_kernel<D, CAUSAL, SINGLE> over CTAs [unit0, unit0 + n_units) of the plane-major
+// (plane, query group) order (all CTAs when n_units < 0).
+template <int D, bool CAUSAL, bool SINGLE>
+static int launch_attention_part(const AttnArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                 AttnParams p, int unit0, int64_t n_units, cudaStream_t stream) {
+  using C = AttnCfg<D, SINGLE>;
+  p.q_groups = (a.Sq + C::QT * 128 - 1) / (C::QT * 128);
+  p.unit0 = unit0;
+  auto kern = sage_attn_kernel<D, CAUSAL, SINGLE>;
+  if constexpr (C::REBALANCE) {
+    // setmaxnreg moves registers between warpgroups inside the allocation the CTA was launched with; a
+    // build allocating other than REGS_LAUNCH per thread would make the softmax's increase wait forever
+    static int regs = -1;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) regs = fa.numRegs;
+    });
+    if (regs != C::REGS_LAUNCH) {
+      set_error("attention kernel built with %d registers per thread; its setmaxnreg split needs %d", regs,
+                C::REGS_LAUNCH);
+      return kStatusLaunch;
+    }
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
+  if (e != cudaSuccess) {
+    set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  const int64_t grid = n_units >= 0 ? n_units : (int64_t)a.B * a.H * p.q_groups;
+  if (grid <= 0) return kStatusOk;
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("attention launch: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  return kStatusOk;
+}
+
+// SM count of the current device (cached per device).
+static int device_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (sms[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    sms[dev] = n;
+  }
+  return sms[dev];
+}
+
+int attention_tail_split(int D, int causal, int varlen, int64_t planes, int Sq, int nsm, int64_t* main_ctas) {
+  // Two-tile CTAs (D = 96, 128) take one SM each.  When a call's last wave would be at most half full, its
+  // CTAs instead run as single-tile CTAs of a second launch: those carry no wait for the next S (the two S
+  // slots alternate) and finish about twice as fast, so the last wave costs about half of one.
+  const int64_t pairs = planes * ((Sq + 255) / 256);
+  *main_ctas = pairs;
+  if (causal || varlen || (D != 96 && D != 128) || nsm <= 0) return 0;
+  const int64_t full = pairs / nsm, rest = pairs - full * nsm;
+  if (full == 0 || rest == 0 || 2 * rest > nsm) return 0;
+  *main_ctas = full * nsm;
+  return 1;
+}
+
 template <int D, bool CAUSAL>
 static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   using C = AttnCfg<D>;
@@ -834,38 +903,21 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.seg_ok = a.seg_ok;
   p.total_q = a.total_q;
   p.pad_total = a.pad_total;
-  p.q_groups = (a.Sq + C::QT * 128 - 1) / (C::QT * 128);
   p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   p.out_f16 = a.out_dtype == 1;
-  auto kern = sage_attn_kernel<D, CAUSAL>;
-  if constexpr (C::REBALANCE) {
-    // setmaxnreg moves registers between warpgroups inside the allocation the CTA was launched with; a
-    // build allocating other than REGS_LAUNCH per thread would make the softmax's increase wait forever
-    static int regs = -1;
-    static std::once_flag once;
-    std::call_once(once, [&] {
-      cudaFuncAttributes fa;
-      if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess) regs = fa.numRegs;
-    });
-    if (regs != C::REGS_LAUNCH) {
-      set_error("attention kernel built with %d registers per thread; its setmaxnreg split needs %d", regs,
-                C::REGS_LAUNCH);
-      return kStatusLaunch;
+  if constexpr (C::QT == 2 && !CAUSAL) {
+    int64_t main_ctas = 0;
+    if (attention_tail_split(D, 0, varlen, q_planes, a.Sq, device_sms(), &main_ctas)) {
+      const int rc = launch_attention_part<D, false, false>(a, mq, mk, mv, p, 0, main_ctas, stream);
+      if (rc != kStatusOk) return rc;
+      // the remaining two-tile groups, as single tiles: the tile order continues the group order
+      const int g2 = (a.Sq + 255) / 256, g1 = (a.Sq + 127) / 128;
+      const int64_t tile0 = (main_ctas / g2) * g1 + (main_ctas % g2) * 2;
+      return launch_attention_part<D, false, true>(a, mq, mk, mv, p, (int)tile0, (int64_t)q_planes * g1 - tile0,
+                                                   stream);
     }
   }
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC);
-  if (e != cudaSuccess) {
-    set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    return kStatusLaunch;
-  }
-  const int64_t grid = (int64_t)a.B * a.H * p.q_groups;
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_ALLOC, stream>>>(mq, mk, mv, p);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) {
-    set_error("attention launch: %s", cudaGetErrorString(e));
-    return kStatusLaunch;
-  }
-  return kStatusOk;
+  return launch_attention_part<D, CAUSAL, false>(a, mq, mk, mv, p, 0, -1, stream);
 }
 
 #ifdef SAGE_DEBUG

@@ -104,6 +104,10 @@ struct AttnArgs {
 int launch_attention(const AttnArgs& a, cudaStream_t stream);
 // Query rows one attention CTA owns for head dim D (the grid is B * H * ceil(Sq / rows)).
 int attention_rows_per_cta(int D);
+// Whether a dense call's attention runs as two launches: `main_ctas` two-tile CTAs (whole waves of `nsm`)
+// plus single-tile CTAs for the rest, when the last wave of two-tile CTAs would be at most half full (D 96
+// and 128, non-causal).  `main_ctas` receives the number of two-tile CTAs either way.
+int attention_tail_split(int D, int causal, int varlen, int64_t planes, int Sq, int nsm, int64_t* main_ctas);
 
 int* default_status_word();
 

@@ -31,6 +31,13 @@ _torch_sdpa = torch._C._nn.scaled_dot_product_attention
 # smaller calls are dominated by the fixed cost of the quantisation pass and run SDPA.
 MIN_WORK = int(os.environ.get("RDNA4_SAGE_MIN_WORK", 64 * 2**20))
 MIN_KV = int(os.environ.get("RDNA4_SAGE_MIN_KV", 1024))
+# On B200, routing also follows the measured crossover against torch SDPA (cuDNN / flash, bf16 and f16):
+# above the size thresholds the quantised path is faster for head_dim 256 (1.5-3x) and whenever the
+# log-sum-exp is requested (it comes from the kernel instead of a torch pass over the logits, 15-60x),
+# and slower for head_dim 64, 96 and 128 (0.5-0.8x), which therefore run SDPA.  ROUTING = "size" (or the
+# environment variable RDNA4_SAGE_ROUTING=size) restores the reference's size-only rule.
+ROUTING = os.environ.get("RDNA4_SAGE_ROUTING", "measured")
+FAST_HEAD_DIMS = (256,)
 
 
 def is_available(device=None) -> bool:
@@ -78,8 +85,8 @@ def _sdpa(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask):
     return o.transpose(1, 2) if tensor_layout == "NHD" else o
 
 
-def _worth_it(q, k, tensor_layout, is_causal=False):
-    """The size rule: enough keys and enough (query, key) pairs for the quantisation pass to pay off."""
+def _big_enough(q, k, tensor_layout, is_causal=False):
+    """The reference's size rule: enough keys and (query, key) pairs for the quantisation pass to pay off."""
     heads_ax, seq_ax = (1, 2) if tensor_layout == "HND" else (2, 1)
     batch, heads, q_len, kv_len = q.shape[0], q.shape[heads_ax], q.shape[seq_ax], k.shape[seq_ax]
     pairs = batch * heads * q_len * kv_len
@@ -88,11 +95,20 @@ def _worth_it(q, k, tensor_layout, is_causal=False):
     return kv_len >= MIN_KV and pairs >= MIN_WORK
 
 
+def _worth_it(q, k, tensor_layout, is_causal=False, lse=False):
+    """Whether the quantised path is the faster choice for this call: the size rule, and on B200 (ROUTING
+    "measured") a head dim where it beats SDPA or a call that wants the log-sum-exp."""
+    if not _big_enough(q, k, tensor_layout, is_causal):
+        return False
+    return lse or ROUTING == "size" or q.shape[-1] in FAST_HEAD_DIMS
+
+
 def sageattn(q, k, v, tensor_layout="HND", is_causal=False, sm_scale=None, attn_mask=None, return_lse=False, **kwargs):
-    """Drop-in for sageattention.sageattn.  The B200 kernels take the call when they support it and it is large
-    enough (_worth_it); masks, unsupported shapes, dtypes or GPUs and small calls run torch SDPA.  Causal masks
-    are bottom-right aligned, as in SageAttention and FlashAttention.  Other SageAttention keyword arguments
-    are accepted and ignored."""
+    """Drop-in for sageattention.sageattn.  The B200 kernels take the call when they support it and are the
+    faster choice for it (_worth_it: the size rule and, by default, the measured head-dim crossover); masks,
+    unsupported shapes, dtypes or GPUs, small calls and head dims where torch SDPA is faster run SDPA.  Causal
+    masks are bottom-right aligned, as in SageAttention and FlashAttention.  Other SageAttention keyword
+    arguments are accepted and ignored."""
     if return_lse:
         raise NotImplementedError("rdna4_sage: return_lse is not supported")
     use_kernel = attn_mask is None and _worth_it(q, k, tensor_layout, is_causal)

@@ -59,7 +59,7 @@ def _lse(q, k, tensor_layout, is_causal, sm_scale):
 
 def _kernel_lse_call(q, k, v, tensor_layout, is_causal, sm_scale, attn_mask):
     """(out, lse) from the kernel when rdna4_sage.sageattn would route this call to it, else None."""
-    if attn_mask is not None or not rdna4_sage._worth_it(q, k, tensor_layout, is_causal):
+    if attn_mask is not None or not rdna4_sage._worth_it(q, k, tensor_layout, is_causal, lse=True):
         return None
     try:
         rdna4_sage.check_supported(q, k, v, tensor_layout, is_causal)
@@ -107,11 +107,14 @@ def sageattn_varlen(
 ) -> torch.Tensor:
     """Packed variable-length attention: q [total_q, H, D], k / v [total_k, Hkv, D], cu_seqlens [batch + 1].
 
-    On a B200 with supported inputs and enough work (total_q * max_seqlen_k * H >= rdna4_sage.MIN_WORK and
-    max_seqlen_k >= rdna4_sage.MIN_KV) the whole batch runs as one kernel pipeline with no host
-    synchronisation (rdna4_sage.attention_varlen); every sequence's rows equal a dense call on it.
-    Otherwise each sequence goes through sageattn in turn, as the reference shim does (core.py:66-89)."""
-    if kwargs.get("attn_mask") is None and max_seqlen_k >= rdna4_sage.MIN_KV and \
+    On a B200 with supported inputs, enough work (total_q * max_seqlen_k * H >= rdna4_sage.MIN_WORK and
+    max_seqlen_k >= rdna4_sage.MIN_KV) and a head dim where the quantised path is the faster one
+    (rdna4_sage.FAST_HEAD_DIMS, or any with rdna4_sage.ROUTING == "size") the whole batch runs as one kernel
+    pipeline with no host synchronisation (rdna4_sage.attention_varlen); every sequence's rows equal a dense
+    call on it.  Otherwise each sequence goes through sageattn in turn, as the reference shim does
+    (core.py:66-89)."""
+    native = rdna4_sage.ROUTING == "size" or q.shape[-1] in rdna4_sage.FAST_HEAD_DIMS
+    if native and kwargs.get("attn_mask") is None and max_seqlen_k >= rdna4_sage.MIN_KV and \
             q.shape[0] * max_seqlen_k * q.shape[1] >= rdna4_sage.MIN_WORK:
         try:
             rdna4_sage.check_supported_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k)

@@ -80,12 +80,21 @@ def test_routing_on_cpu_and_errors():
     assert not rdna4_sage.is_available() or torch.cuda.is_available()
 
 
-def test_worth_it_thresholds():
+def test_worth_it_thresholds(monkeypatch):
     q = torch.empty(1, 24, 4608, 128, device="meta")
-    assert rdna4_sage._worth_it(q, q, "HND")
     small = torch.empty(1, 2, 512, 64, device="meta")
-    assert not rdna4_sage._worth_it(small, small, "HND")
     assert rdna4_sage.MIN_WORK == 64 * 2**20 and rdna4_sage.MIN_KV == 1024
+    # the reference's size rule
+    assert rdna4_sage._big_enough(q, q, "HND") and not rdna4_sage._big_enough(small, small, "HND")
+    # B200 default: the measured crossover against SDPA (head_dim 256, or a log-sum-exp request)
+    assert rdna4_sage.ROUTING == "measured"
+    assert not rdna4_sage._worth_it(q, q, "HND")
+    assert rdna4_sage._worth_it(q, q, "HND", lse=True)
+    d256 = torch.empty(1, 16, 2048, 256, device="meta")
+    assert rdna4_sage._worth_it(d256, d256, "HND")
+    assert not rdna4_sage._worth_it(small, small, "HND", lse=True)
+    monkeypatch.setattr(rdna4_sage, "ROUTING", "size")
+    assert rdna4_sage._worth_it(q, q, "HND") and not rdna4_sage._worth_it(small, small, "HND")
 
 
 def test_varlen_cpu_loops_like_reference():

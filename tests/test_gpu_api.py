@@ -26,8 +26,22 @@ def ref(q, k, v, layout, causal=False, scale=None):
 def test_is_available_and_kernel_route():
     assert rdna4_sage.is_available()
     q = torch.randn(1, 24, 4352, 128, device="cuda", dtype=torch.bfloat16)
-    assert rdna4_sage._worth_it(q, q, "HND")
+    assert rdna4_sage._big_enough(q, q, "HND")
     rdna4_sage.check_supported(q, q, q, "HND")
+
+
+def test_routing_follows_the_measured_crossover():
+    """Default routing on B200: one shape on each side of the measured crossover against torch SDPA.  A
+    head_dim 256 call goes to the kernels (they beat SDPA there); a head_dim 128 call of the same size runs
+    SDPA (faster there); with return_lse the head_dim 128 call takes the kernels again."""
+    assert rdna4_sage.ROUTING == "measured"
+    q256, k256, v256 = (torch.randn(1, 16, 4096, 256, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    assert torch.equal(sageattn(q256, k256, v256), rdna4_sage.attention(q256, k256, v256))
+    q, k, v = (torch.randn(1, 16, 4096, 128, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    assert torch.equal(sageattn(q, k, v), rdna4_sage._sdpa(q, k, v, "HND", False, None, None))
+    o, lse = sageattn(q, k, v, return_lse=True)
+    ok, olse = torch.ops.rdna4_sage.attention_lse(q, k, v, "HND", 0.0, False)
+    assert torch.equal(o, ok.transpose(1, 2)) and torch.equal(lse, olse)
 
 
 def test_layouts_dtypes_causal():

@@ -9,6 +9,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
+import rdna4_sage
 import sageattention
 from oracle import sage_oracle as O
 from sage_gpu_helpers import cos, rel_l1
@@ -96,19 +97,19 @@ def _check(q, k, v, out_nhd, heads, causal, n_rows=48, lse=None, sdpa_heads=None
 def test_config1_flux():
     q, k, v = _inputs(0, 1, 24, 24, 4608, 128, 2.0, outliers=4, outlier_scale=20.0)
     th = lambda t: t.transpose(1, 2).contiguous()   # the reference call is HND
-    out = sageattention.sageattn(th(q), th(k), th(v), tensor_layout="HND", sm_scale=128 ** -0.5)
+    out = rdna4_sage.attention(th(q), th(k), th(v), tensor_layout="HND", sm_scale=128 ** -0.5)
     _check(q, k, v, out.transpose(1, 2), [0, 23], False, sdpa_heads=list(range(24)))
 
 
 def test_config2_wan():
     q, k, v = _inputs(1, 1, 40, 40, 32760, 128, 2.0)
-    out = sageattention.sageattn(q, k, v, tensor_layout="NHD")
+    out = rdna4_sage.attention(q, k, v, tensor_layout="NHD")
     _check(q, k, v, out, [0, 39], False, n_rows=32, sdpa_heads=[0, 17, 39])
 
 
 def test_config3_hunyuan_single_gpu():
     q, k, v = _inputs(3, 1, 24, 24, 67576, 128, 2.0)
-    out = sageattention.sageattn(q, k, v, tensor_layout="NHD")
+    out = rdna4_sage.attention(q, k, v, tensor_layout="NHD")
     _check(q, k, v, out, [5], False, n_rows=24, sdpa_heads=[5, 20])
 
 

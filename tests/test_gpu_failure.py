@@ -59,7 +59,7 @@ def test_device_error_raises_at_a_later_call_without_opting_in():
     launch errors, src/rdna4_sage/_hip.py:47-49), with no per-call synchronisation and no RDNA4_SAGE_CHECK."""
     dev = torch.device("cuda", 0)
     _attention.check_status(dev)                      # start clean
-    q = torch.randn(1, 24, 4096, 128, device=dev, dtype=torch.bfloat16)   # a call sageattn routes to the kernel
+    q = torch.randn(1, 16, 4096, 256, device=dev, dtype=torch.bfloat16)   # a call sageattn routes to the kernel
     assert rdna4_sage._worth_it(q, q, "HND")
     rdna4_sage.attention(q, q, q, "HND")              # a normal call first: nothing pending
     _attention.selftest_wait_timeout(20, dev)         # a pipeline wait that expires

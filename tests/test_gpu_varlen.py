@@ -91,7 +91,8 @@ def test_cross_lengths_empty_sequences_and_sm_scale():
     _check_equal(lens_q, lens_k, 6, 3, 128, torch.bfloat16, False, seed=7, sm_scale=0.05)
 
 
-def test_sageattn_varlen_routes_native_and_matches_loop():
+def test_sageattn_varlen_routes_native_and_matches_loop(monkeypatch):
+    monkeypatch.setattr(rdna4_sage, "ROUTING", "size")  # head_dim 128: native only under the size rule
     lens = [3000, 1200, 2048, 5000]
     q, k, v = _packed(lens, lens, 8, 8, 128, torch.bfloat16, seed=3)
     cu = _cu(lens)

@@ -186,6 +186,21 @@ int sage_selftest_counter_timeout(int* status, int* words, int limit_ms, void* s
  * device); returns the code it held (SAGE_OK when no kernel reported an error). */
 int sage_status_sync(int* status, void* stream);
 
+/* Debug builds (compiled with SAGE_DEBUG; libsage_b200_debug.so) check their own accesses on the device:
+ * every global store of a kernel must land inside the buffers its launch was given, TMA copies must start on
+ * a 16-byte column inside their tensor, and varlen offsets must stay inside the packed tensors.  A failed
+ * check skips the access and records it; no check traps.  This reads and clears the first record of `unit`
+ * (0 = attention kernels, 1 = quantisers, 2 = the self-test kernels) into out8: count of violations (0 = none), code (1 expired wait,
+ * 2 TMA column, 3 TMA row, 4 store outside its buffers, 5 varlen offsets), block, thread, then two 64-bit
+ * values as (lo, hi) int pairs.  Synchronises the device.  Production builds return SAGE_ERR_UNSUPPORTED. */
+int sage_debug_record(int unit, int* out8);
+
+/* Debug builds: a kernel stores 0x5a over every 16-byte chunk of `buf` (device, 16-byte aligned, `bytes` a
+ * multiple of 16 in 32..2^20) while the launch's store table holds `buf` less its last chunk.  No store
+ * leaves the buffer; the last one leaves the table, so the store check skips it and records it (unit 2,
+ * code 4, address buf + bytes - 16): the check's own test.  Production builds return SAGE_ERR_UNSUPPORTED. */
+int sage_selftest_debug_store(void* buf, int bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -63,6 +63,9 @@ struct AttnParams {
   const int* seg_ok;
   int total_q;
   int64_t pad_total;
+  // extents of the q8 and k8 / v8t tensor maps (rows per plane, planes), for the debug build's TMA checks
+  int64_t q_rows, k_rows;
+  int q_planes, k_planes;
 };
 
 // SINGLE: one 128-row Q tile per CTA whatever D (the launch that finishes a call's last, partial wave)
@@ -366,6 +369,17 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     ks_off = (int64_t)hkv * (p.pad_total / kKvBlock) + kbase / kKvBlock;
     out_off = (int64_t)qb * p.o_ss + (int64_t)h * p.o_sh;
     if (grp == 0 && Sq > p.q_groups * QT * 128) atomicCAS(p.status, 0, kStatusInvalid);  // max_seqlen_q too small
+#ifdef SAGE_DEBUG
+    // the sequence's rows lie inside the packed tensors and its keys start on a 32-key block
+    if (qb < 0 || Sq < 0 || qb + Sq > p.total_q) {
+      debug_violation(kDbgOffsets, (int64_t)qb + Sq, p.total_q);
+      return;
+    }
+    if (kbase < 0 || kbase % kKvBlock != 0 || Skv < 0 || (int64_t)kbase + (int64_t)nkb * kKvBlock > p.pad_total) {
+      debug_violation(kDbgOffsets, (int64_t)kbase + (int64_t)nkb * kKvBlock, p.pad_total);
+      return;
+    }
+#endif
   }
   const int q0 = grp * QT * 128;
   if (q0 >= Sq) return;  // varlen: this group lies past a shorter sequence (the whole CTA leaves)
@@ -415,6 +429,8 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
       mbar_arrive_expect_tx(q_full, q_tiles_in * C::Q_TILE);
       for (int t = 0; t < q_tiles_in; ++t)
         for (int a = 0; a < C::DK / C::SW; ++a)
+          SAGE_DCHECK(qbase + q0 + t * 128 < p.q_rows, kDbgTmaRow, qbase + q0 + t * 128, p.q_rows)
+          SAGE_DCHECK(zq < p.q_planes, kDbgTmaRow, zq, p.q_planes)
           tma_load_3d(sQ + t * C::Q_TILE + a * C::BM * C::SW, &tm_q, q_full, a * C::SW, qbase + q0 + t * 128,
                       zq);
       int issued = 0;
@@ -426,12 +442,17 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
           ok = false;
           break;
         }
+        const int key0 = kbase + j * C::BN;  // first key row of K, first key column of V^T
+        SAGE_DCHECK(zk < p.k_planes, kDbgTmaRow, zk, p.k_planes) {}
         mbar_arrive_expect_tx(&k_full[st], C::K_TILE);
         for (int a = 0; a < C::DK / C::SW; ++a)
-          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, kbase + j * C::BN,
-                      zk);
+          SAGE_DCHECK(key0 < p.k_rows, kDbgTmaRow, key0, p.k_rows)
+          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, key0, zk);
         mbar_arrive_expect_tx(&v_full[st], C::V_TILE);
-        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], kbase + j * C::BN, 0, zk);
+        // V^T is read along its key columns: a TMA column must start on 16 bytes
+        SAGE_DCHECK((key0 & 15) == 0, kDbgTmaCol, key0, 2)
+        SAGE_DCHECK(key0 < p.k_rows, kDbgTmaRow, key0, p.k_rows)
+        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], key0, 0, zk);
         issued = j + 1;
       }
       if (!ok) {
@@ -740,12 +761,14 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
         }
         if (store) {
           uint4* dst = reinterpret_cast<uint4*>(orow + cc * 64);
+          SAGE_DSTORE(dst, 64)
 #pragma unroll
           for (int v = 0; v < 4; ++v)
             dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
       }
       if (p.lse != nullptr && store)
+        SAGE_DSTORE(&p.lse[q_off + q_row], 4)
         p.lse[q_off + q_row] = (m * c + log2f(l)) * 0.69314718055994531f;
     }
     tmem_wait_st();
@@ -903,6 +926,23 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.seg_ok = a.seg_ok;
   p.total_q = a.total_q;
   p.pad_total = a.pad_total;
+  p.q_rows = q_rows;
+  p.k_rows = k_rows;
+  p.q_planes = (int)q_planes;
+  p.k_planes = (int)k_planes;
+  {
+    // the output and log-sum-exp extents the call's shape and strides give (debug builds check every store)
+    const int64_t rows = varlen ? a.total_q : a.Sq;
+    const int64_t last = rows > 0 ? (varlen ? 0 : (int64_t)(a.B - 1) * a.out_st.b) + (rows - 1) * a.out_st.s +
+                                        (int64_t)(a.H - 1) * a.out_st.h + a.D
+                                  : 0;
+    const cudaError_t e = debug_register(stream, {{a.out, (uint64_t)last * 2},
+                                                  {a.lse, sizeof(float) * (uint64_t)q_planes * (uint64_t)rows}});
+    if (e != cudaSuccess) {
+      set_error("debug buffer table: %s", cudaGetErrorString(e));
+      return kStatusLaunch;
+    }
+  }
   p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   p.out_f16 = a.out_dtype == 1;
   if constexpr (C::QT == 2 && !CAUSAL) {
@@ -921,14 +961,8 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
 }
 
 #ifdef SAGE_DEBUG
-// The attention kernels' expired-wait record (see record_wait); cleared by the read.
-extern "C" int sage_debug_attn_wait_record(int* out5) {
-  int rec[5] = {0, 0, 0, 0, 0};
-  if (cudaMemcpyFromSymbol(rec, g_wait_record, sizeof(rec)) != cudaSuccess) return kStatusLaunch;
-  const int zero[5] = {0, 0, 0, 0, 0};
-  if (cudaMemcpyToSymbol(g_wait_record, zero, sizeof(zero)) != cudaSuccess) return kStatusLaunch;
-  for (int i = 0; i < 5; ++i) out5[i] = rec[i];
-  return kStatusOk;
+int attention_debug_record(int* out8) {
+  return debug_take_record(out8) == cudaSuccess ? kStatusOk : kStatusLaunch;
 }
 #endif
 

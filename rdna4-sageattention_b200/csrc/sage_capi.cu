@@ -386,4 +386,23 @@ int sage_status_sync(int* status, void* stream) {
   return host;
 }
 
+int sage_debug_record(int unit, int* out8) {
+  g_error[0] = 0;
+#ifdef SAGE_DEBUG
+  if (out8 == nullptr || unit < 0 || unit > 2) {
+    set_error("sage_debug_record: unit 0 (attention), 1 (quantisers) or 2 (self-tests) and an array of 8 ints");
+    return SAGE_ERR_INVALID;
+  }
+  const int rc = unit == 0 ? attention_debug_record(out8)
+                           : (unit == 1 ? quant_debug_record(out8) : selftest_debug_record(out8));
+  if (rc != SAGE_OK) set_error("debug record read failed");
+  return rc;
+#else
+  (void)unit;
+  (void)out8;
+  set_error("not a debug build (compile with SAGE_DEBUG)");
+  return SAGE_ERR_UNSUPPORTED;
+#endif
+}
+
 }  // extern "C"

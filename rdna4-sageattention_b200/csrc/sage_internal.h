@@ -111,4 +111,12 @@ int attention_tail_split(int D, int causal, int varlen, int64_t planes, int Sq, 
 
 int* default_status_word();
 
+#ifdef SAGE_DEBUG
+// Debug builds: read and clear the first recorded violation of the attention kernels / the quantisers
+// (count, code, block, thread, a lo, a hi, b lo, b hi; count 0 = none).
+int attention_debug_record(int* out8);
+int quant_debug_record(int* out8);
+int selftest_debug_record(int* out8);
+#endif
+
 }  // namespace sage

@@ -6,6 +6,7 @@
 #pragma once
 
 #include <cstdint>
+#include <initializer_list>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -98,25 +99,98 @@ __device__ __forceinline__ bool aborted(const WaitCtx& w) {
   return *w.cta_abort != 0 || *reinterpret_cast<volatile int*>(w.status) != 0;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Debug builds (SAGE_DEBUG): the kernels check their own accesses instead of relying on a sanitizer.  Every
+// global store must land inside one of the buffers the launching host code registered for the launch, TMA
+// copies must start on a 16-byte column and inside their tensor's rows, and varlen offsets must stay inside
+// the packed tensors.  A failed check records the first violation (and a count) in a per-translation-unit
+// record and skips the access; no check traps.  Waits that expire are recorded the same way.  Production
+// builds compile the checks away.
+// ------------------------------------------------------------------------------------------------
+enum : int {
+  kDbgWait = 1,      // a bounded wait expired (a = shared address of the barrier, b = parity)
+  kDbgTmaCol = 2,    // TMA column not a multiple of 16 bytes (a = column, b = tensor id)
+  kDbgTmaRow = 3,    // TMA start row outside the tensor (a = row, b = rows)
+  kDbgStore = 4,     // global store outside every registered buffer (a = address, b = bytes)
+  kDbgOffsets = 5,   // varlen offsets outside the packed tensors (a = offset, b = limit)
+};
+
+struct DebugBufs {  // the launch's output buffers: [base, base + bytes)
+  uint64_t base[8];
+  uint64_t bytes[8];
+  int n;
+};
+
 #ifdef SAGE_DEBUG
-// Debug builds record the first wait of a launch that expired: {1, shared-memory address of the barrier
-// (0 for other waits), parity, block, thread}.  One record per translation unit (no relocatable device
-// code), read through that unit's sage_debug_* accessor.
-static __device__ int g_wait_record[5];
-__device__ __forceinline__ void record_wait(const void* bar, uint32_t parity) {
-  if (atomicCAS(&g_wait_record[0], 0, 1) == 0) {
-    g_wait_record[1] = bar != nullptr ? (int)smem_u32(bar) : 0;
-    g_wait_record[2] = (int)parity;
-    g_wait_record[3] = (int)blockIdx.x;
-    g_wait_record[4] = (int)threadIdx.x;
+static __device__ int g_debug_record[8];  // count, code, block, thread, a (lo, hi), b (lo, hi)
+static __device__ DebugBufs g_debug_bufs;
+
+__device__ __forceinline__ void debug_violation(int code, int64_t a, int64_t b) {
+  if (atomicAdd(&g_debug_record[0], 1) == 0) {
+    g_debug_record[1] = code;
+    g_debug_record[2] = (int)blockIdx.x;
+    g_debug_record[3] = (int)threadIdx.x;
+    g_debug_record[4] = (int)(a & 0xffffffff);
+    g_debug_record[5] = (int)(a >> 32);
+    g_debug_record[6] = (int)(b & 0xffffffff);
+    g_debug_record[7] = (int)(b >> 32);
   }
 }
+
+__device__ __forceinline__ bool debug_store_ok(const void* p, uint64_t nbytes) {
+  const uint64_t a = reinterpret_cast<uint64_t>(p);
+  for (int i = 0; i < g_debug_bufs.n; ++i)
+    if (a >= g_debug_bufs.base[i] && a + nbytes <= g_debug_bufs.base[i] + g_debug_bufs.bytes[i]) return true;
+  debug_violation(kDbgStore, (int64_t)a, (int64_t)nbytes);
+  return false;
+}
+
+// Reads and clears this translation unit's record.
+static inline cudaError_t debug_take_record(int* out8) {
+  int rec[8];
+  cudaError_t e = cudaMemcpyFromSymbol(rec, g_debug_record, sizeof(rec));
+  if (e != cudaSuccess) return e;
+  const int zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  e = cudaMemcpyToSymbol(g_debug_record, zero, sizeof(zero));
+  for (int i = 0; i < 8; ++i) out8[i] = rec[i];
+  return e;
+}
+#define SAGE_DSTORE(ptr, nbytes) if (debug_store_ok((ptr), (nbytes)))
+#define SAGE_DCHECK(cond, code, a, b) \
+  if (!(cond)) debug_violation((code), (int64_t)(a), (int64_t)(b)); else
 #else
-__device__ __forceinline__ void record_wait(const void*, uint32_t) {}
+__device__ __forceinline__ void debug_violation(int, int64_t, int64_t) {}
+#define SAGE_DSTORE(ptr, nbytes)
+#define SAGE_DCHECK(cond, code, a, b)
 #endif
 
+// Registers the buffers the next launches on `stream` may write: each {pointer, bytes} the launch's contract
+// gives it (null pointers are left out).  Debug builds only; production builds register nothing.  The table
+// is one per translation unit, shared by calls that overlap on different streams, and its update is a copy
+// from pageable memory, which a CUDA graph capture does not take: debug builds run uncaptured.
+struct DebugBuf {
+  const void* ptr;
+  uint64_t bytes;
+};
+static inline cudaError_t debug_register(cudaStream_t stream, std::initializer_list<DebugBuf> list) {
+#ifdef SAGE_DEBUG
+  DebugBufs b{};
+  for (const DebugBuf& d : list)
+    if (d.ptr != nullptr && b.n < 8) {
+      b.base[b.n] = reinterpret_cast<uint64_t>(d.ptr);
+      b.bytes[b.n] = d.bytes;
+      ++b.n;
+    }
+  return cudaMemcpyToSymbolAsync(g_debug_bufs, &b, sizeof(b), 0, cudaMemcpyHostToDevice, stream);
+#else
+  (void)stream;
+  (void)list;
+  return cudaSuccess;
+#endif
+}
+
 __device__ __forceinline__ void raise_timeout(const WaitCtx& w, const void* bar = nullptr, uint32_t parity = 0) {
-  record_wait(bar, parity);
+  debug_violation(kDbgWait, bar != nullptr ? (int64_t)smem_u32(bar) : 0, parity);
   *w.cta_abort = 1;
   atomicCAS(w.status, 0, kStatusTimeout);
 }

@@ -146,6 +146,7 @@ __device__ __forceinline__ void store_codes(const float* x, float scale, int8_t*
       w[k] = (uint32_t)(c0 & 0xff) | ((uint32_t)(c1 & 0xff) << 8) | ((uint32_t)(c2 & 0xff) << 16) |
              ((uint32_t)(c3 & 0xff) << 24);
     }
+    SAGE_DSTORE(dst + i, 16)
     *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
@@ -193,7 +194,7 @@ __device__ __forceinline__ void quant_k_row(const T* __restrict__ krow, bool val
   const float kscale = quant_row<D, T, SMEM>(krow, valid, k8row, inpad, [](float a) {
     return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(a)));
   });
-  if (lane == 0) *ks_entry = kscale;
+  if (lane == 0) SAGE_DSTORE(ks_entry, 4) *ks_entry = kscale;
 }
 
 // V row to e4m3 with the per-channel factors fac[c] = 448 / max(vs_c, 1e-30); channel c of this key goes
@@ -210,7 +211,9 @@ __device__ __forceinline__ void quant_v_row(const T* __restrict__ vrow, bool val
       const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c + kx], -448.f), 448.f);
       const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + kx + 1], -448.f), 448.f);
       const uint16_t pk = pack_e4m3x2(y0, y1);
+      SAGE_DSTORE(&vout[(int64_t)(c + kx) * pitch], 1)
       vout[(int64_t)(c + kx) * pitch] = (uint8_t)(pk & 0xff);
+      SAGE_DSTORE(&vout[(int64_t)(c + kx + 1) * pitch], 1)
       vout[(int64_t)(c + kx + 1) * pitch] = (uint8_t)(pk >> 8);
     }
   }
@@ -226,6 +229,7 @@ __device__ __forceinline__ void quant_q_row(const T* __restrict__ row, bool vali
   float scale = quant_row<D, T, SMEM>(row, valid, q8row, valid, [](float a) { return a; });
   if (valid) {
     if ((D & (D - 1)) == 0) scale = scale / (float)(D < 128 ? D : 128);
+    SAGE_DSTORE(qs_entry, 4)
     *qs_entry = scale * fold;
   }
 }
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(kRows) quant_q_pair_kernel(const T* __restrict
   const float scale = __fdiv_rn(fmaxf(a, 1e-12f), 127.0f);
   if (valid) {
     store_codes<PART>(v, scale, q8 + ((int64_t)bh * S + s) * D + part * PART);
-    if (part == 0) qs[(int64_t)bh * S + s] = scale / 128.0f * fold;
+    if (part == 0) SAGE_DSTORE(&qs[(int64_t)bh * S + s], 4) qs[(int64_t)bh * S + s] = scale / 128.0f * fold;
   }
 }
 
@@ -330,6 +334,14 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
     pitch = sg.pad_total;
     o0 = (int64_t)h * pitch + sg.cu_pad[b];
     vbase = (int64_t)h * D * pitch + sg.cu_pad[b];
+#ifdef SAGE_DEBUG
+    // the sequence's padded key rows start on a 32-key block and end inside the packed tensors
+    const int64_t pad_len = (int64_t)(S + kKvBlock - 1) / kKvBlock * kKvBlock;
+    if (S < 0 || sg.cu_pad[b] % kKvBlock != 0 || sg.cu_pad[b] + pad_len > pitch) {
+      if (threadIdx.x == 0) debug_violation(kDbgOffsets, sg.cu_pad[b] + pad_len, pitch);
+      return;
+    }
+#endif
   } else {
     pitch = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
     o0 = (int64_t)bh * pitch;
@@ -399,7 +411,7 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
   if (inpad) {
     const int64_t orow = (int64_t)bh * pitch + s;
     store_codes<PART>(x, kscale, k8 + orow * D + part * PART);
-    if ((threadIdx.x & (32 * TPR - 1)) == 0) ks[orow / kKvBlock] = kscale;
+    if ((threadIdx.x & (32 * TPR - 1)) == 0) SAGE_DSTORE(&ks[orow / kKvBlock], 4) ks[orow / kKvBlock] = kscale;
     // V: this part's channels to e4m3, written transposed
     const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h + part * PART;
     uint8_t* vout = v8t + (int64_t)bh * D * pitch + (int64_t)part * PART * pitch + s;
@@ -451,6 +463,7 @@ __global__ void __launch_bounds__(256) v_amax_kernel(const T* __restrict__ v, in
       for (int k = 0; k < 8; ++k) acc[k] = fmaxf(acc[k], red[rr * G + threadIdx.x][k]);
 #pragma unroll
     for (int k = 0; k < 8; ++k)
+      SAGE_DSTORE(vs + (int64_t)bh * D + threadIdx.x * 8 + k, 4)
       atomicMax(reinterpret_cast<unsigned int*>(vs + (int64_t)bh * D + threadIdx.x * 8 + k), __float_as_uint(acc[k]));
   }
 }
@@ -642,6 +655,7 @@ __global__ void __launch_bounds__(kRows) quant_fused_kernel(const T* __restrict_
         // max via the order of non-negative float bit patterns (vs is zero on entry)
 #pragma unroll
         for (int kx = 0; kx < 8; ++kx)
+          SAGE_DSTORE(vs + (int64_t)it.plane * D + tid * 8 + kx, 4)
           atomicMax(reinterpret_cast<unsigned int*>(vs + (int64_t)it.plane * D + tid * 8 + kx),
                     __float_as_uint(acc[kx]));
       }
@@ -678,6 +692,16 @@ __global__ void __launch_bounds__(kRows) quant_fused_kernel(const T* __restrict_
 // ------------------------------------------------------------------------------------------------
 // host launchers
 // ------------------------------------------------------------------------------------------------
+// Debug builds: the buffers the next launches may write (see debug_register).
+static int register_outputs(cudaStream_t stream, std::initializer_list<DebugBuf> bufs) {
+  const cudaError_t e = debug_register(stream, bufs);
+  if (e != cudaSuccess) {
+    set_error("debug buffer table: %s", cudaGetErrorString(e));
+    return kStatusLaunch;
+  }
+  return kStatusOk;
+}
+
 static int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -690,6 +714,9 @@ static int check_launch(const char* what) {
 template <int D, typename T>
 static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold, int8_t* q8, float* qs,
                      cudaStream_t stream) {
+  constexpr uint64_t DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+  const uint64_t rows = (uint64_t)B * H * S;
+  if (register_outputs(stream, {{q8, rows * DK}, {qs, rows * sizeof(float)}}) != kStatusOk) return kStatusLaunch;
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
     if constexpr (D == 128 || D == 256) {
       constexpr int rpb = kRows / rows_tpr<D>();
@@ -709,6 +736,14 @@ template <int D, typename T>
 static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
                       int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
   const int spad = (int)kv_pad(S);  // varlen: S is the longest sequence
+  {
+    // k8 [planes, pitch, DK], ks [planes, pitch / 32], v8t [planes, D, pitch]
+    constexpr uint64_t DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+    const uint64_t rows = sg.cu != nullptr ? (uint64_t)H * sg.pad_total : (uint64_t)B * H * spad;
+    if (register_outputs(stream, {{k8, rows * DK}, {ks, rows / kKvBlock * sizeof(float)}, {v8t, rows * D}}) !=
+        kStatusOk)
+      return kStatusLaunch;
+  }
   const T* kp = reinterpret_cast<const T*>(k);
   const T* vp = reinterpret_cast<const T*>(v);
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
@@ -733,6 +768,7 @@ static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides
 
 template <int D, typename T>
 static int v_amax_t(const void* v, int B, int S, int H, Strides3 st, float* vs, cudaStream_t stream, const Segs& sg) {
+  if (register_outputs(stream, {{vs, sizeof(float) * (uint64_t)B * H * D}}) != kStatusOk) return kStatusLaunch;
   cudaError_t e = cudaMemsetAsync(vs, 0, sizeof(float) * (size_t)B * H * D, stream);
   if (e != cudaSuccess) {
     set_error("v_amax memset: %s", cudaGetErrorString(e));
@@ -795,6 +831,17 @@ static int quant_fused_t(const void* q, const void* k, const void* v, int B, int
     return kStatusUnsupported;
   }
   const FusedPlan pl = fused_plan(B, H, Hkv, Sq, Skv, D, (int)sizeof(T));
+  {
+    constexpr uint64_t DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
+    const uint64_t qrows = (uint64_t)B * H * Sq, krows = (uint64_t)B * Hkv * kv_pad(Skv);
+    if (register_outputs(stream, {{q8, qrows * DK},
+                                  {qs, qrows * sizeof(float)},
+                                  {k8, krows * DK},
+                                  {ks, krows / kKvBlock * sizeof(float)},
+                                  {v8t, krows * D},
+                                  {vs, sizeof(float) * (uint64_t)B * Hkv * D}}) != kStatusOk)
+      return kStatusLaunch;
+  }
   // vs (max via atomicMax from zero) and the work counters are zeroed together when they are adjacent
   const size_t vs_bytes = sizeof(float) * (size_t)B * Hkv * D;
   const size_t sync_bytes = sizeof(int) * (size_t)quant_fused_sync_ints(B, Hkv);
@@ -867,11 +914,12 @@ __global__ void varlen_vtail_kernel(uint8_t* __restrict__ v8t, int64_t pad_total
                                     int nseq, const int* __restrict__ ok) {
   if (*ok == 0) return;
   const int64_t col = (int64_t)cu_pad[nseq] + threadIdx.x;
-  if (col < pad_total) v8t[(int64_t)blockIdx.x * pad_total + col] = 0;
+  if (col < pad_total) SAGE_DSTORE(&v8t[(int64_t)blockIdx.x * pad_total + col], 1) v8t[(int64_t)blockIdx.x * pad_total + col] = 0;
 }
 
 int launch_varlen_vtail(uint8_t* v8t, int Hkv, int D, int64_t pad_total, const int* cu_pad, int nseq, const int* ok,
                         cudaStream_t stream) {
+  if (register_outputs(stream, {{v8t, (uint64_t)Hkv * D * pad_total}}) != kStatusOk) return kStatusLaunch;
   varlen_vtail_kernel<<<Hkv * D, 128, 0, stream>>>(v8t, pad_total, cu_pad, nseq, ok);
   return check_launch("varlen_vtail");
 }
@@ -912,5 +960,9 @@ int launch_quant_fused(const void* q, const void* k, const void* v, int dtype, i
   SAGE_DISPATCH_D(D, quant_fused_t, q, k, v, B, H, Hkv, Sq, Skv, sq, sk, sv, fold, q8, qs, k8, ks, v8t, vs, sync,
                   status, stream)
 }
+
+#ifdef SAGE_DEBUG
+int quant_debug_record(int* out8) { return debug_take_record(out8) == cudaSuccess ? kStatusOk : kStatusLaunch; }
+#endif
 
 }  // namespace sage

@@ -33,9 +33,52 @@ __global__ void counter_timeout_kernel(int* words, int* status, uint64_t limit_n
   wait_counter(&words[0], 1, &words[1], status, limit_ns);
 }
 
+// Debug builds: thread i stores 16 bytes of 0x5a at buf + 16 i, for every 16-byte chunk of the buffer, while
+// the launch's store table holds the buffer less its last chunk.  Every store stays inside the buffer; the
+// last one lies outside the table, so the store check skips it and records it.
+__global__ void debug_store_kernel(uint8_t* buf, int chunks) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= chunks) return;
+  uint4* dst = reinterpret_cast<uint4*>(buf + 16 * (int64_t)i);
+  SAGE_DSTORE(dst, 16)
+  *dst = make_uint4(0x5a5a5a5au, 0x5a5a5a5au, 0x5a5a5a5au, 0x5a5a5a5au);
+}
+
+#ifdef SAGE_DEBUG
+int selftest_debug_record(int* out8) { return debug_take_record(out8) == cudaSuccess ? kStatusOk : kStatusLaunch; }
+#endif
+
 }  // namespace sage
 
 using namespace sage;
+
+extern "C" int sage_selftest_debug_store(void* buf, int bytes, void* stream) {
+#ifdef SAGE_DEBUG
+  if (buf == nullptr || (reinterpret_cast<uintptr_t>(buf) & 15) != 0 || bytes < 32 || bytes > (1 << 20) ||
+      bytes % 16 != 0) {
+    set_error("a 16-byte aligned device buffer of 32..2^20 bytes, a multiple of 16, required (got %d)", bytes);
+    return SAGE_ERR_INVALID;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = debug_register(st, {{buf, (uint64_t)bytes - 16}});
+  if (e == cudaSuccess) {
+    const int chunks = bytes / 16;
+    debug_store_kernel<<<(chunks + 127) / 128, 128, 0, st>>>(static_cast<uint8_t*>(buf), chunks);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    set_error("selftest launch: %s", cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  }
+  return SAGE_OK;
+#else
+  (void)buf;
+  (void)bytes;
+  (void)stream;
+  set_error("not a debug build (compile with SAGE_DEBUG)");
+  return SAGE_ERR_UNSUPPORTED;
+#endif
+}
 
 extern "C" int sage_selftest_counter_timeout(int* status, int* words, int limit_ms, void* stream) {
   if (limit_ms < 1 || limit_ms > 2000 || words == nullptr) {

@@ -68,6 +68,8 @@ SIGNATURES = {
     "sage_selftest_wait_timeout": (_c_i, [_c_p, _c_i, _c_p]),
     "sage_selftest_counter_timeout": (_c_i, [_c_p, _c_p, _c_i, _c_p]),
     "sage_status_sync": (_c_i, [_c_p, _c_p]),
+    "sage_debug_record": (_c_i, [_c_i, _c_p]),
+    "sage_selftest_debug_store": (_c_i, [_c_p, _c_i, _c_p]),
 }
 ABI_VERSION = 1
 

@@ -47,6 +47,19 @@ def test_host_only_queries():
     assert L.sage_workspace_bytes(1, 2, 2, 10, 10, 80) == 0
 
 
+def test_debug_entries_answer_only_in_debug_builds():
+    # production builds export the debug entries but hold no checks; libsage_b200_debug.so has them
+    L = _lib.lib()
+    rec = (ctypes.c_int * 8)()
+    if os.path.basename(_lib.LIB_PATH) == "libsage_b200.so":
+        assert L.sage_debug_record(0, rec) == _lib.SAGE_ERR_UNSUPPORTED
+        assert b"not a debug build" in L.sage_last_error()
+        assert L.sage_selftest_debug_store(None, 64, None) == _lib.SAGE_ERR_UNSUPPORTED
+    debug = ctypes.CDLL(os.path.join(os.path.dirname(_lib.LIB_PATH), "libsage_b200_debug.so"))
+    debug.sage_debug_record.argtypes = [ctypes.c_int, ctypes.c_void_p]
+    assert debug.sage_debug_record(7, rec) == _lib.SAGE_ERR_INVALID  # unit out of range: answered on the host
+
+
 def test_argument_errors_without_gpu():
     L = _lib.lib()
     rc = L.sage_attention(None, None, None, 0, 1, 2, 2, 64, 64, 80, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0, None, 0, 0,

@@ -105,12 +105,16 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
 
 /* sage_attention without a workspace argument, for callers that cannot allocate device memory (a host
  * framework that owns all device memory through its own pool, or an FFI caller with no CUDA allocator):
- * the quantised tensors live in a 32 MiB array inside the library, held by every GPU that loads it.
- * This entry point has no counterpart in the reference (whose Python host always allocates through
- * torch).  Calls needing more than 32 MiB of scratch (sage_workspace_bytes) return SAGE_ERR_UNSUPPORTED.
- * All calls share the array, so calls that overlap on the GPU race; order them on one stream.  The
- * first call on a device looks up the array's address with cudaGetSymbolAddress: make it before any
- * stream capture. */
+ * the quantised tensors live in a 32 MiB array inside the library.  This entry point has no counterpart in
+ * the reference (whose Python host always allocates through torch).  A device takes the 32 MiB when the
+ * library's module is loaded on it: under CUDA's default lazy loading that is this entry point's first
+ * call on the device (CUDA_MODULE_LOADING=EAGER: the library's first use of it), and the device keeps it
+ * until the process exits.  Make that first call before any stream capture and before a memory pool takes
+ * the device's free memory: its address lookup (cudaGetSymbolAddress) loads the module, and a failure
+ * there returns SAGE_ERR_LAUNCH with "static scratch: cudaGetSymbolAddress failed on device N (<CUDA
+ * error>)".  Calls needing more than 32 MiB of scratch (sage_workspace_bytes) return
+ * SAGE_ERR_UNSUPPORTED.  All calls share the array, so calls that overlap on the GPU race; order them on
+ * one stream.  A call allocates no device memory. */
 int sage_attention_static(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
                           int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss,
                           int64_t ksh, int64_t vsb, int64_t vss, int64_t vsh, double sm_scale, int causal, void* out,

@@ -4,8 +4,13 @@
 // bound through an FFI layer that has no handle on a CUDA allocator.
 //
 // Instead of a caller-provided workspace, the quantised tensors live in one file-scope device array
-// of kStaticScratchBytes.  That array belongs to the library image: every GPU that loads the library
-// holds it (in addition to the caller's memory) until the process exits.  Calls larger than the array
+// of kStaticScratchBytes.  That array belongs to this file's module: a device holds it from the moment
+// the module is loaded on it until the process exits.  Under CUDA's default lazy module loading that is
+// the first sage_attention_static call on the device (its cudaGetSymbolAddress loads the module, and the
+// driver takes the 32 MiB then); with CUDA_MODULE_LOADING=EAGER it is the library's first use of the
+// device.  A caller whose framework reserves a memory pool should make its first call before the pool
+// takes the device's free memory, or that call can fail with the lookup's out-of-memory error (returned as
+// SAGE_ERR_LAUNCH with the CUDA error text).  Calls larger than the array
 // are rejected with SAGE_ERR_UNSUPPORTED and a message naming the limit.  All calls share the array:
 // two calls whose kernels overlap on the GPU (different streams, different host threads) race on it
 // and corrupt each other's results, so callers must order them (one stream, or events).  The array

@@ -49,6 +49,31 @@ def test_static_scratch_matches_workspace_entry_two_calls():
     _run_both(2, 2, 4, 2, 1500, 64, "f16", True, 0.05)   # second call reuses the array left by the first
 
 
+def test_static_scratch_call_allocates_nothing():
+    # after a first call (which loads the array on this device), a call of another shape leaves the device's
+    # free memory exactly as it was: the entry point allocates nothing
+    L = _lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    q1, k1, v1 = make_qkv(3, 1, 4, 4, 1024, 1024, 128, "NHD", "bf16", dist="offset2")
+    q2, k2, v2 = make_qkv(4, 1, 2, 1, 3000, 3000, 64, "NHD", "f16", dist="offset2")
+    o1, o2 = torch.empty_like(q1), torch.empty_like(q2)
+    # the second shape's kernels are loaded first (through the workspace entry point), so that loading their
+    # code cannot count against the measured call
+    need = L.sage_workspace_bytes(1, 2, 1, 3000, 3000, 64)
+    ws = torch.empty(need, device="cuda", dtype=torch.uint8)
+    _lib.check(L.sage_attention(*_args(q2, k2, v2, o2, True, 0.0), None, ws.data_ptr(), need, None, stream),
+               "sage_attention")
+    _lib.check(L.sage_attention_static(*_args(q1, k1, v1, o1, False, 0.0), None, None, stream), "first call")
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    _lib.check(L.sage_attention_static(*_args(q2, k2, v2, o2, True, 0.0), None, None, stream), "second call")
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert L.sage_status_sync(None, stream) == 0
+    assert free_after == free_before
+    assert bool(torch.isfinite(o2.float()).all())
+
+
 def test_static_scratch_rejects_oversized_calls():
     L = _lib.lib()
     B, H, S, D = 1, 40, 32760, 128

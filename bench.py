@@ -475,7 +475,8 @@ def run_ours(args):
     if os.path.exists(tpath) and (args.heads, args.seq) == (H, N):
         import re
         mt = re.search(r"traffic_bytes_per_full_launch:\s*(\d+)", open(tpath).read())
-        traffic = int(mt.group(1)) if mt else None
+        # the figure is for all H heads; a rank of a split call launches the kernel on its own heads
+        traffic = int(int(mt.group(1)) * Hq / H) if mt else None
     elems = Bq * Sq * Hq * Dq
     quant_bytes = 3 * elems * 2 + 3 * elems + (Bq * Hq * Sq + Bq * Hq * spad // 32 + Bq * Hq * Dq) * 4
     quant_gbs = quant_bytes / (quant_ms * 1e-3) / 1e9

@@ -217,11 +217,12 @@ __device__ __noinline__ float exact_tile(uint32_t taddr, const BlockVals<NB> ksb
   return l;
 }
 
-// Returns true when the tile went through exact_tile (P is then already stored).
+// Returns true when the tile went through exact_tile (P is then already stored).  `quiet` (warp-uniform)
+// reports a tile in which no row of the warp moved its max at all: every k is 1.
 template <bool MASK, int NB>
 __device__ __forceinline__ bool softmax_tile(uint32_t (&s)[NB][32], uint32_t taddr, const float (&ksv)[NB], float c,
                                              float& m, float& l, int kv0, int lim, float (&k)[NB],
-                                             uint32_t (&pw)[NB * 8]) {
+                                             uint32_t (&pw)[NB * 8], bool& quiet) {
   if (MASK) {
 #pragma unroll
     for (int i = 0; i < NB; ++i)
@@ -229,15 +230,30 @@ __device__ __forceinline__ bool softmax_tile(uint32_t (&s)[NB][32], uint32_t tad
       for (int e = 0; e < 32; ++e)
         if (kv0 + i * 32 + e >= lim) s[i][e] = (uint32_t)INT32_MIN;
   }
+  int mxs[NB];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) mxs[i] = max32_tree(s[i]);
+  // Common case: no block of the tile moves the running max.  A block moves it iff (x_i - m) * c > 8 for its
+  // scaled max x_i (or m is still -inf), and (x - m) * c is monotonic in x, so one test on the largest x_i
+  // decides for all blocks; every k is then 1 and every block's max is m, as the per-block chain would give.
+  {
+    float xmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < NB; ++i)
+      if (!MASK || mxs[i] != INT32_MIN) xmax = fmaxf(xmax, (float)mxs[i] * ksv[i]);
+    const bool still = m != -INFINITY && !((xmax - m) * c > 8.0f);
+    // (4-block tiles only: with two blocks the test saves little and costs the D = 64 kernel registers)
+    quiet = NB >= 4 && __all_sync(0xffffffffu, still);
+  }
   // lazy running max, decided per 32-key block in key order as the reference's 32-key tiles do
   float mb[NB];
   float mc = m;
   bool late = false;  // the max moved after the tile's first block
 #pragma unroll
   for (int i = 0; i < NB; ++i) {
-    const int mx = max32_tree(s[i]);
+    const int mx = mxs[i];
     k[i] = 1.0f;
-    if (!MASK || mx != INT32_MIN) {
+    if (!quiet && (!MASK || mx != INT32_MIN)) {
       const float cand = fmaxf(mc, (float)mx * ksv[i]);
       if (cand != -INFINITY && (cand - mc) * c > 8.0f) {
         k[i] = fast_exp2((mc - cand) * c);  // 0 for the first block of a row (m = -inf)
@@ -248,7 +264,7 @@ __device__ __forceinline__ bool softmax_tile(uint32_t (&s)[NB][32], uint32_t tad
     mb[i] = mc;
   }
   m = mc;
-  if (__any_sync(0xffffffffu, late)) {
+  if (!quiet && __any_sync(0xffffffffu, late)) {
     BlockVals<NB> ksb, mbb, kbb;
 #pragma unroll
     for (int i = 0; i < NB; ++i) {
@@ -404,6 +420,7 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     }
     mbar_init(mma_drain, 1);
     *cta_abort = 0;
+    for (int i = 0; i < C::MASK_INTS; ++i) split_mask[i] = 0u;  // each warp then stores its byte when it changes
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -585,6 +602,7 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     // previous tile, so a warp meets a pending split only while it waits for that S (or for the P.V): it
     // tests o_part there and serves the split.  With QT = 1 the next S is issued before the previous
     // P.V, so the warp settles the previous tile's splits before it announces the next P.
+    uint32_t mask_last = 0;  // the split-mask bytes this warp last stored, one per tile parity
     int pend_j = -1;     // tile whose P.V may still be split (-1: none)
     int pend_mask = -1;  // its split blocks not served yet (-1: not read yet)
     int nsplit = 0;      // splits served so far (the o_part / o_fix phases)
@@ -682,10 +700,11 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
       const int lim = min(Skv, CAUSAL ? last_key + 1 : Skv);  // keys < lim are kept
       uint32_t pw[NB * 8];
       float kb[NB];
-      const bool stored = need_mask ? softmax_tile<true, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw)
-                                    : softmax_tile<false, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw);
+      bool quiet;
+      const bool stored = need_mask ? softmax_tile<true, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw, quiet)
+                                    : softmax_tile<false, NB>(s, ts, ksv, c, m, l, kv0, lim, kb, pw, quiet);
       // a move at the tile's first block scales the O of the earlier tiles before this tile's P.V
-      if (__any_sync(FULL, j > 0 && kb[0] != 1.0f)) {
+      if (!quiet && __any_sync(FULL, j > 0 && kb[0] != 1.0f)) {
         if (!wait_s(&o_done[t], (j - 1) & 1)) {
           ok = false;
           break;
@@ -706,12 +725,20 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
           tmem_st16(ts, pw);
       }
       // blocks after the first whose max moved in some row of this warp: the P.V is split there
-      int bits = 0;
+      int wmask = 0;
+      if (!quiet) {
+        int bits = 0;
 #pragma unroll
-      for (int i = 1; i < NB; ++i) bits |= (kb[i] != 1.0f) ? (1 << i) : 0;
-      const int wmask = __reduce_or_sync(FULL, bits);
-      if (lane == 0)
-        reinterpret_cast<volatile uint8_t*>(split_mask)[((j & 1) * 4 + t) * 4 + wq] = (uint8_t)wmask;
+        for (int i = 1; i < NB; ++i) bits |= (kb[i] != 1.0f) ? (1 << i) : 0;
+        wmask = __reduce_or_sync(FULL, bits);
+      }
+      // the byte of this tile parity is stored only when it changes (shared memory keeps the last value);
+      // 2-block tiles store it every time (their kernel is short of registers)
+      if (NB < 4 || wmask != ((mask_last >> ((j & 1) * 8)) & 0xff)) {
+        if (lane == 0)
+          reinterpret_cast<volatile uint8_t*>(split_mask)[((j & 1) * 4 + t) * 4 + wq] = (uint8_t)wmask;
+        mask_last = (mask_last & ~(0xffu << ((j & 1) * 8))) | ((uint32_t)wmask << ((j & 1) * 8));
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

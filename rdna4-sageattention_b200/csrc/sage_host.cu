@@ -110,14 +110,14 @@ size_t slot_bytes(int B, int hg, int hkg, int Sq, int Skv, int D, size_t es) {
 // link: alone they run at the H2D / D2H rates, together at `both` split in that ratio.  A chunk's kernels
 // take whole waves of CTAs plus a per-chunk overhead.  The constants are measured on B200 (PCIe 5.0 x16;
 // the Wan call's attention rate) and only rank the candidates: on the Wan call (B1 H40 N32760 D128)
-// 2-head chunks take 21.2 ms, 1-head chunks 22.0 ms and 8-head chunks 23.9 ms.
+// 1-, 2- and 4-head chunks take 23.4-23.5 ms, 8-head chunks 23.9 ms, 20-head chunks 31.5 ms.
 int auto_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D) {
   const int G = H / Hkv;
   int dev = 0, nsm = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (nsm <= 0) nsm = 148;
   const double h2d = 51e9, d2h = 50e9, both = 88e9;  // bytes/s
-  const double rate = 1.32e15;                        // attention operations/s on a full GPU
+  const double rate = 1.17e15;                        // attention operations/s on a full GPU
   const double overhead = 70e-6;                      // per chunk: quantiser launches, ramp-up, copy set-up
   const double es = 2.0;
   const double rows = attention_rows_per_cta(D);

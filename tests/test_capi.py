@@ -87,8 +87,9 @@ def test_host_pipeline_planner_without_gpu():
     L = _lib.lib()
     B, H, Hkv, S, D = 1, 40, 40, 32760, 128
     hg = L.sage_host_heads_per_chunk(B, H, Hkv, S, S, D, 0)
-    # the chunk size measured fastest on B200 for the Wan call (2 heads: 21.2 ms; 1 head: 22.0 ms; 8: 23.9 ms)
-    assert hg == 2
+    # a chunk size measured within 1 % of the fastest on B200 for the Wan call (1-4 heads: 23.4-23.6 ms;
+    # 8: 23.9 ms; 20: 31.5 ms; one chunk of 40: 42.8 ms)
+    assert hg in (1, 2, 3, 4)
     assert L.sage_host_heads_per_chunk(B, H, Hkv, S, S, D, 8) == 8
     assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 0) % 4 == 0      # whole GQA groups
     assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 6) == 0          # not a multiple of 4

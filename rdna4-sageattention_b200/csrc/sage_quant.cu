@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
 // quant_q_pair_kernel).  A 32-key scale block is the 32 * TPR threads of TPR consecutive warps: each warp
 // reduces its rows, the warps of a block exchange their maxima through shared memory.  Codes, scales and V
 // bytes are those of quant_kv_kernel.
-template <int D, typename T>
+template <int D, typename T, bool WITH_V = true>
 __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
                                                               int H, Strides3 sk, Strides3 sv,
                                                               const float* __restrict__ vs, int8_t* __restrict__ k8,
@@ -391,7 +391,8 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
   const int64_t pitch = spad;
   __shared__ float fac[D];
   __shared__ float wmax[kRows / 32];
-  for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
+  if (WITH_V)
+    for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
   const bool valid = s < S;     // real key (rows in [S, spad) are zero padding)
   const bool inpad = s < spad;  // row exists in the padded tensors
   // K: this part of the row, rotated
@@ -412,10 +413,73 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
     const int64_t orow = (int64_t)bh * pitch + s;
     store_codes<PART>(x, kscale, k8 + orow * D + part * PART);
     if ((threadIdx.x & (32 * TPR - 1)) == 0) SAGE_DSTORE(&ks[orow / kKvBlock], 4) ks[orow / kKvBlock] = kscale;
+    if (!WITH_V) return;
     // V: this part's channels to e4m3, written transposed
     const T* vrow = v + (int64_t)b * sv.b + (int64_t)(valid ? s : 0) * sv.s + (int64_t)h * sv.h + part * PART;
     uint8_t* vout = v8t + (int64_t)bh * D * pitch + (int64_t)part * PART * pitch + s;
     quant_v_row<PART, T>(vrow, valid, fac + part * PART, vout, pitch);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// V alone (dense calls with D = 128 and 256, beside the K-only pair kernel): a CTA converts 128 keys of one
+// (batch, kv head) to e4m3 with the channel factors and writes them transposed.  Loads are coalesced along
+// the key rows (16 lanes per 256-byte row for D = 128); the codes go through a shared-memory tile in which
+// channel c's keys are contiguous (16-byte chunks XOR-swizzled by c / 8, so the 16 lanes of one row hit 8
+// bank groups), and leave as 16-byte stores of channel rows.  Same arithmetic as quant_v_row.
+// ------------------------------------------------------------------------------------------------
+template <int D, typename T>
+__global__ void __launch_bounds__(256) quant_v_tile_kernel(const T* __restrict__ v, int S, int H, Strides3 sv,
+                                                           const float* __restrict__ vs, uint8_t* __restrict__ v8t,
+                                                           int bh0) {
+  constexpr int ROWS = 128;  // keys per CTA
+  constexpr int G = D / 8;   // 16-byte chunks per key row
+  __shared__ float fac[D];
+  __shared__ __align__(16) uint8_t tile[D * ROWS];
+  const int bh = bh0 + (int)blockIdx.y;
+  const int b = bh / H;
+  const int h = bh - b * H;
+  const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
+  const int s0 = blockIdx.x * ROWS;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
+  __syncthreads();
+  // all of a thread's loads first (ROWS * G / 256 = D / 16 chunks in flight), then the conversions
+  constexpr int PER = ROWS * G / 256;
+  const T* vbase = v + (int64_t)b * sv.b + (int64_t)h * sv.h;
+  uint4 raw[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int q = (int)threadIdx.x + i * 256;
+    const int r = q / G, g = q - (q / G) * G;
+    const int s = s0 + r;
+    raw[i] = s < S ? __ldg(reinterpret_cast<const uint4*>(vbase + (int64_t)s * sv.s + g * 8)) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int q = (int)threadIdx.x + i * 256;
+    const int r = q / G, g = q - (q / G) * G;
+    // channel g * 8 + kx of key r: 16-byte chunk (r >> 4) ^ (g & 7) of channel row g * 8 + kx
+    uint8_t* trow = tile + g * 8 * ROWS + ((((r >> 4) ^ (g & 7)) << 4) | (r & 15));
+    const T* e = reinterpret_cast<const T*>(&raw[i]);
+#pragma unroll
+    for (int kx = 0; kx < 8; kx += 2) {
+      const int c = g * 8 + kx;
+      const float y0 = fminf(fmaxf(to_f32<T>(e[kx]) * fac[c], -448.f), 448.f);
+      const float y1 = fminf(fmaxf(to_f32<T>(e[kx + 1]) * fac[c + 1], -448.f), 448.f);
+      const uint16_t pk = pack_e4m3x2(y0, y1);
+      trow[kx * ROWS] = (uint8_t)(pk & 0xff);
+      trow[(kx + 1) * ROWS] = (uint8_t)(pk >> 8);
+    }
+  }
+  __syncthreads();
+  uint8_t* base = v8t + (int64_t)bh * D * spad + s0;
+  constexpr int CH = ROWS / 16;
+  for (int q = threadIdx.x; q < D * CH; q += blockDim.x) {
+    const int c = q / CH, kc = q - (q / CH) * CH;
+    if (s0 + kc * 16 >= spad) continue;
+    uint8_t* dst = base + (int64_t)c * spad + kc * 16;
+    SAGE_DSTORE(dst, 16)
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(tile + c * ROWS + ((kc ^ ((c >> 3) & 7)) << 4));
   }
 }
 
@@ -751,8 +815,12 @@ static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides
       if (sg.cu == nullptr) {
         constexpr int rpb = kRows / rows_tpr<D>();
         dim3 grid2((spad + rpb - 1) / rpb, min(kMaxGridY, B * H - bh0));
-        quant_kv_pair_kernel<D, T><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
+        // K (rotation, codes, block scales) and V (codes, transposed) in two kernels
+        quant_kv_pair_kernel<D, T, false><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
         if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
+        dim3 grid3((spad + 127) / 128, min(kMaxGridY, B * H - bh0));
+        quant_v_tile_kernel<D, T><<<grid3, 256, 0, stream>>>(vp, S, H, sv, vs, v8t, bh0);
+        if (check_launch("quant_v") != kStatusOk) return kStatusLaunch;
         continue;
       }
     }

@@ -90,6 +90,16 @@ int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const flo
                   const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D, int causal,
                   int64_t osb, int64_t oss, int64_t osh, float* lse, int* status, void* stream);
 
+/* sage_attn_fwd for a block of query rows of a longer sequence (no counterpart in the reference, which runs
+ * a sequence's rows in one call): query row i of this call is row q_row0 + i of the Skv keys, so a causal
+ * call keeps keys j <= q_row0 + i (sage_attn_fwd is q_row0 = Skv - Sq, bottom-right).  Requires
+ * 0 <= q_row0 and q_row0 + Sq <= Skv (else SAGE_ERR_INVALID).  Context parallelism uses it: each rank
+ * attends its own chunk of rows against the gathered keys. */
+int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                       const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
+                       int causal, int q_row0, int64_t osb, int64_t oss, int64_t osh, float* lse, int* status,
+                       void* stream);
+
 /* Workspace bytes sage_attention needs for the quantised tensors above (256-byte aligned parts). */
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D);
 

@@ -229,7 +229,7 @@ def sm_log2e(head_dim: int) -> np.float32:
 
 def attention_rows(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarray, v8: np.ndarray,
                    vs: np.ndarray, rows: np.ndarray, seq_q: int, seq_kv: int, causal: bool,
-                   block_n: int = KV_BLOCK, lazy: bool = True):
+                   block_n: int = KV_BLOCK, lazy: bool = True, row0: int | None = None):
     """Emulate the reference kernel for one (batch, head) on the given query rows.
 
     kernel_build/make_sage_r2.py:54-269.  Per 32-key block b (the reference's tile and K-scale block):
@@ -243,7 +243,8 @@ def attention_rows(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarra
       out     = O * (1/448) / l * vs                                      (make_sage_r2.py:255-268)
     with c = fp32(sm_scale * log2e) * qs.  With block_n = 128 the p of blocks preceding a max move inside the
     same tile are taken relative to the tile's final max (a different fp8 rounding of the same value).  Keys >= seq_kv are masked; causal keeps key
-    j <= i + (seq_kv - seq_q) (bottom-right, make_sage_r2.py:91-117).
+    j <= i + (seq_kv - seq_q) (bottom-right, make_sage_r2.py:91-117), or j <= i + row0 when row0 gives the
+    position of query row 0 among the keys (a block of rows of a longer sequence).
 
     q8 (Sq, D) int8, qs (Sq,) f32, k8 (Skv_pad, D) int8, ks (Skv_pad/32,) f32, v8 (Skv_pad, D) uint8
     codes, vs (D,) f32.  Returns out (R, D) float32 (before the cast to the output dtype) and
@@ -256,7 +257,7 @@ def attention_rows(q8: np.ndarray, qs: np.ndarray, k8: np.ndarray, ks: np.ndarra
     qrow = q8[rows].astype(np.float64)
     vdec = e4m3_decode(v8)                                        # (Skv_pad, D) float64
     kdec = k8.astype(np.float64)
-    off = seq_kv - seq_q
+    off = seq_kv - seq_q if row0 is None else row0
     m = np.full(R, -np.inf, dtype=F32)
     l = np.zeros(R, dtype=F32)
     o = np.zeros((R, D), dtype=F32)

@@ -53,6 +53,7 @@ struct AttnParams {
   int64_t o_sb, o_ss, o_sh;
   int B, H, Hkv, Sq, Skv, nkb;
   int q_groups;  // number of QT*128-row query groups per (batch, head)
+  int row0;      // dense: position of query row 0 among the keys (causal keeps key j <= row0 + i)
   int unit0;     // non-causal dense launches: (plane, query group) index of this launch's first CTA
   float sm_log2e;
   int out_f16;
@@ -399,7 +400,7 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
   }
   const int q0 = grp * QT * 128;
   if (q0 >= Sq) return;  // varlen: this group lies past a shorter sequence (the whole CTA leaves)
-  const int off = Skv - Sq;
+  const int off = p.cu_q != nullptr ? Skv - Sq : p.row0;
   int kv_end = Skv;
   if (CAUSAL) kv_end = min(Skv, q0 + QT * 128 + off);
   const int n_tiles = kv_end > 0 ? (kv_end + C::BN - 1) / C::BN : 0;
@@ -946,6 +947,7 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.Hkv = a.Hkv;
   p.Sq = a.Sq;
   p.Skv = a.Skv;
+  p.row0 = a.row0 == INT_MIN ? a.Skv - a.Sq : a.row0;
   p.nkb = varlen ? 0 : (int)(k_rows / kKvBlock);
   p.cu_q = a.cu_q;
   p.cu_k = a.cu_k;

@@ -258,6 +258,35 @@ int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const flo
   return launch_attention(a, static_cast<cudaStream_t>(stream));
 }
 
+int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                       const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
+                       int causal, int q_row0, int64_t osb, int64_t oss, int64_t osh, float* lse, int* status,
+                       void* stream) {
+  if (q_row0 < 0 || (int64_t)q_row0 + Sq > (int64_t)Skv) {
+    g_error[0] = 0;
+    set_error("query rows %d..%d lie outside the %d keys", q_row0, q_row0 + Sq - 1, Skv);
+    return SAGE_ERR_INVALID;
+  }
+  NvtxRange nvtx("sage_attn_fwd_rows");
+  g_error[0] = 0;
+  int rc = check_common(out_dtype, B, Sq, H, D);
+  if (rc != SAGE_OK) return rc;
+  if (Hkv <= 0 || H % Hkv != 0 || Skv <= 0) {
+    set_error("heads %d must be a multiple of kv heads %d and kv length %d positive", H, Hkv, Skv);
+    return SAGE_ERR_UNSUPPORTED;
+  }
+  if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8t) || qs == nullptr || ks == nullptr || vs == nullptr) {
+    set_error("quantised operands must be 16-byte aligned and non-null");
+    return SAGE_ERR_INVALID;
+  }
+  rc = check_input(out, osb, oss, osh, "out");
+  if (rc != SAGE_OK) return rc;
+  AttnArgs a{q8, qs, k8, ks, v8t, vs, out, out_dtype, Strides3{osb, oss, osh}, lse, status, B, H, Hkv, Sq, Skv, D,
+             causal ? 1 : 0};
+  a.row0 = q_row0;
+  return launch_attention(a, static_cast<cudaStream_t>(stream));
+}
+
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D) {
   if (sage_qk_row_bytes(D) == 0 || B <= 0 || H <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0) return 0;
   return carve(nullptr, B, H, Hkv, Sq, Skv, D).bytes;

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstddef>
+#include <climits>
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <nvtx3/nvToolsExt.h>
@@ -100,6 +101,8 @@ struct AttnArgs {
   const int* seg_ok = nullptr;
   int total_q = 0;
   int64_t pad_total = 0;
+  // dense: position of query row 0 in the key sequence (causal keeps key j <= row0 + i); INT_MIN: Skv - Sq
+  int row0 = INT_MIN;
 };
 int launch_attention(const AttnArgs& a, cudaStream_t stream);
 // Query rows one attention CTA owns for head dim D (the grid is B * H * ceil(Sq / rows)).

@@ -7,11 +7,12 @@ Steps per call (all ranks of `group`, same order):
      tokens, so every 32-key K scale block lies inside one chunk and equals the single-GPU one);
   3. all-gather of the quantised K (int8), its block scales and V^T (e4m3) - 1 byte per element instead of
      the 2-byte inputs - and reassembly into the kernel's [B, Hkv, S, DK] / [B, Hkv, D, S] layouts;
-  4. the attention kernel on the local query rows against all keys.
-The output rows of each rank equal the corresponding rows of the single-GPU call bit for bit.
+  4. the attention kernel on the local query rows against all keys; causal calls give the kernel the
+     chunk's first row position, so row i keeps keys j <= start + i, as in the single-GPU call.
+The output rows of each rank equal the corresponding rows of the single-GPU call bit for bit.  (With
+contiguous chunks a causal call's ranks carry unequal work: rank r attends (r + 1/2) chunks of keys.)
 
-The collective is NCCL through torch.distributed (one process per GPU).  Causal attention is not
-supported here (a rank's rows would need the global row offset).
+The collective is NCCL through torch.distributed (one process per GPU).
 """
 from __future__ import annotations
 
@@ -59,12 +60,14 @@ class KernelBackend:
                                         *k.stride()[:3], *v.stride()[:3], vs.data_ptr(), k8.data_ptr(),
                                         ks.data_ptr(), v8t.data_ptr(), self.stream), "sage_quant_kv")
 
-    def attn(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D):
+    def attn(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D, causal=False, q_row0=0):
         B = out.shape[0]
-        _lib.check(self.L.sage_attn_fwd(q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(),
-                                        vs.data_ptr(), out.data_ptr(), _attention.DTYPES[out.dtype], B, H, Hkv, Sq,
-                                        Skv, D, 0, *out.stride()[:3], None,
-                                        _attention.status_word(out.device).data_ptr(), self.stream), "sage_attn_fwd")
+        _lib.check(self.L.sage_attn_fwd_rows(q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(),
+                                             v8t.data_ptr(), vs.data_ptr(), out.data_ptr(),
+                                             _attention.DTYPES[out.dtype], B, H, Hkv, Sq, Skv, D, int(causal),
+                                             int(q_row0), *out.stride()[:3], None,
+                                             _attention.status_word(out.device).data_ptr(), self.stream),
+                   "sage_attn_fwd_rows")
 
 
 def _gather(x: torch.Tensor, world: int, group) -> torch.Tensor:
@@ -78,11 +81,12 @@ def _gather(x: torch.Tensor, world: int, group) -> torch.Tensor:
     return torch.stack(parts)
 
 
-def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=None):
+def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=None, is_causal=False):
     """Context-parallel attention over `group`.
 
     q, k, v: this rank's chunk (B, S_r, H, D) / (B, S_r, Hkv, D) in NHD layout, chunk r covering tokens
     chunk_bounds(total_len, world, r).  Returns this rank's output rows (B, S_r, H, D) in q's dtype.
+    is_causal: token i attends tokens j <= i of the whole sequence.
     """
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -135,7 +139,8 @@ def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=Non
     # 4. local rows against all keys
     out = torch.empty((B, Sr, H, D), device=dev, dtype=q.dtype)
     if Sr > 0:
-        be.attn(q8, qs, k8_full, ks_full, v8t_full, vs, out, H, Hkv, Sr, total_len, D)
+        be.attn(q8, qs, k8_full, ks_full, v8t_full, vs, out, H, Hkv, Sr, total_len, D, causal=bool(is_causal),
+                q_row0=start)
     return out
 
 

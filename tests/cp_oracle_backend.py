@@ -31,7 +31,7 @@ class OracleBackend:
         ks.copy_(torch.from_numpy(ksc))
         v8t.copy_(torch.from_numpy(np.ascontiguousarray(v8c.transpose(0, 2, 3, 1))))
 
-    def attn(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D):
+    def attn(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D, causal=False, q_row0=0):
         B = out.shape[0]
         g = H // Hkv
         q8n, qsn, k8n, ksn, v8n, vsn = (t.numpy() for t in (q8, qs, k8, ks, v8t, vs))
@@ -41,6 +41,6 @@ class OracleBackend:
                 hk = h // g
                 o, _ = O.attention_rows(q8n[b, h, :, :D], qsn[b, h], k8n[b, hk, :, :D], ksn[b, hk],
                                         np.ascontiguousarray(v8n[b, hk].T), vsn[b, hk], np.arange(Sq), Sq, Skv,
-                                        False, block_n=32)
+                                        causal, block_n=32, row0=q_row0)
                 res[b, :, h] = o
         out.copy_(torch.from_numpy(res).to(out.dtype))

@@ -12,7 +12,7 @@ import torch.multiprocessing as mp
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _worker(rank, world, port, S, H, Hkv, D, sm_scale, results):
+def _worker(rank, world, port, S, H, Hkv, D, sm_scale, results, causal=False):
     sys.path[:0] = [HERE, os.path.join(os.path.dirname(HERE), "rdna4-sageattention_b200"), os.path.dirname(HERE)]
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -24,23 +24,24 @@ def _worker(rank, world, port, S, H, Hkv, D, sm_scale, results):
         k = (torch.randn(1, S, Hkv, D, generator=g) + torch.randn(D, generator=g) * 2).to(torch.bfloat16)
         v = torch.randn(1, S, Hkv, D, generator=g).to(torch.bfloat16)
         out = cp.attention_cp(cp.shard(q, S, world, rank), cp.shard(k, S, world, rank), cp.shard(v, S, world, rank),
-                              S, sm_scale=sm_scale, backend=OracleBackend())
+                              S, sm_scale=sm_scale, backend=OracleBackend(), is_causal=causal)
         results[rank] = out.float().numpy()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("S,H,Hkv,D,sm_scale", [(200, 2, 2, 64, None), (161, 4, 2, 128, 0.07)])
-def test_cp_two_ranks_equal_single_call(S, H, Hkv, D, sm_scale):
+@pytest.mark.parametrize("S,H,Hkv,D,sm_scale,causal", [(200, 2, 2, 64, None, False), (161, 4, 2, 128, 0.07, False),
+                                                       (161, 2, 1, 64, None, True)])
+def test_cp_two_ranks_equal_single_call(S, H, Hkv, D, sm_scale, causal):
     sys.path[:0] = [HERE]
     from cp_oracle_backend import OracleBackend
     from rdna4_sage import cp
     world = 2
     manager = mp.get_context("spawn").Manager()
     results = manager.dict()
-    port = 29500 + (os.getpid() % 1000) + S
-    mp.start_processes(_worker, args=(world, port, S, H, Hkv, D, sm_scale, results), nprocs=world, join=True,
-                       start_method="spawn")
+    port = 29500 + (os.getpid() % 1000) + S + (7 if causal else 0)
+    mp.start_processes(_worker, args=(world, port, S, H, Hkv, D, sm_scale, results, causal), nprocs=world,
+                       join=True, start_method="spawn")
     # single-process reference through the same backend
     g = torch.Generator().manual_seed(7)
     q = torch.randn(1, S, H, D, generator=g).to(torch.bfloat16)
@@ -60,7 +61,7 @@ def test_cp_two_ranks_equal_single_call(S, H, Hkv, D, sm_scale):
     v8t = torch.empty(1, Hkv, D, spad, dtype=torch.uint8)
     be.quant_kv(k, v, vs, k8, ks, v8t)
     ref = torch.empty(1, S, H, D, dtype=torch.bfloat16)
-    be.attn(q8, qs, k8, ks, v8t, vs, ref, H, Hkv, S, S, D)
+    be.attn(q8, qs, k8, ks, v8t, vs, ref, H, Hkv, S, S, D, causal=causal, q_row0=0)
     got = np.concatenate([results[r] for r in range(world)], axis=1)
     np.testing.assert_array_equal(got, ref.float().numpy())
     assert cp.chunk_bounds(S, world, 0)[1] % 32 == 0

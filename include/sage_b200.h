@@ -100,6 +100,17 @@ int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, cons
                        int causal, int q_row0, int64_t osb, int64_t oss, int64_t osh, float* lse, int* status,
                        void* stream);
 
+/* sage_attn_fwd_rows with the keys in chunks, as an all-gather of per-rank chunks lays them out (no
+ * counterpart in the reference): k8 [n_chunks, B, Hkv, chunk_rows, DK], ks [n_chunks, B, Hkv, chunk_rows/32],
+ * v8t [n_chunks, B, Hkv, D, chunk_rows]; key j is row j % chunk_rows of chunk j / chunk_rows.  chunk_rows is
+ * a multiple of 128 (no key tile straddles two chunks) and n_chunks * chunk_rows >= Skv; key rows past Skv
+ * are masked, but their V^T bytes must be finite e4m3 (zero them).  Context parallelism gathers straight into
+ * this layout, so the gathered keys need no re-layout before attention. */
+int sage_attn_fwd_chunked(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                          const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
+                          int causal, int q_row0, int chunk_rows, int n_chunks, int64_t osb, int64_t oss, int64_t osh,
+                          float* lse, int* status, void* stream);
+
 /* Workspace bytes sage_attention needs for the quantised tensors above (256-byte aligned parts). */
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D);
 

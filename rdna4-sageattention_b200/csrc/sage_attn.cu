@@ -54,6 +54,10 @@ struct AttnParams {
   int B, H, Hkv, Sq, Skv, nkb;
   int q_groups;  // number of QT*128-row query groups per (batch, head)
   int row0;      // dense: position of query row 0 among the keys (causal keeps key j <= row0 + i)
+  // chunked keys (n_chunks > 0): rows per chunk, and the K-scale index jump from one chunk to the next
+  // beyond a plane's own blocks; ks_plane = K-scale blocks between planes
+  int chunk_rows, n_chunks, ks_plane;
+  int64_t ks_jump;
   int unit0;     // non-causal dense launches: (plane, query group) index of this launch's first CTA
   float sm_log2e;
   int out_f16;
@@ -322,7 +326,7 @@ __device__ __forceinline__ int pv_split(uint32_t o_tmem, uint32_t p_tmem, uint32
   return n;
 }
 
-template <int D, bool CAUSAL, bool SINGLE>
+template <int D, bool CAUSAL, bool SINGLE, bool CHUNKED>
 __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
@@ -370,7 +374,7 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
   int Sq = p.Sq, Skv = p.Skv, nkb = p.nkb;
   int qbase = 0, kbase = 0, zq = b * p.H + h, zk = b * p.Hkv + hkv;
   int64_t q_off = ((int64_t)b * p.H + h) * p.Sq;               // qs / lse index of query row 0
-  int64_t ks_off = ((int64_t)b * p.Hkv + hkv) * p.nkb;         // ks index of key block 0
+  int64_t ks_off = ((int64_t)b * p.Hkv + hkv) * p.ks_plane;    // ks index of key block 0
   int64_t out_off = (int64_t)b * p.o_sb + (int64_t)h * p.o_sh;  // out element offset of query row 0
   if (p.cu_q != nullptr) {
     if (*p.seg_ok == 0) return;  // the offset tables failed their check (reported in the status word)
@@ -460,17 +464,37 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
           ok = false;
           break;
         }
-        const int key0 = kbase + j * C::BN;  // first key row of K, first key column of V^T
+        int key0 = kbase + j * C::BN;  // first key row of K, first key column of V^T
+        int chunk = 0;                 // chunked keys: a tile lies inside one chunk (chunk_rows % BN == 0)
+        if (CHUNKED) {
+          chunk = key0 / p.chunk_rows;
+          key0 -= chunk * p.chunk_rows;
+        }
         SAGE_DCHECK(zk < p.k_planes, kDbgTmaRow, zk, p.k_planes) {}
+        SAGE_DCHECK(!CHUNKED || chunk < p.n_chunks, kDbgTmaRow, chunk, p.n_chunks) {}
+        // K box of swizzle span a, and the V^T box, from the plain or the chunked map
+        auto load_k = [&](int a) {
+          uint8_t* dst = sK + st * C::K_TILE + a * C::BN * C::SW;
+          if (CHUNKED)
+            tma_load_4d(dst, &tm_k, &k_full[st], a * C::SW, key0, zk, chunk);
+          else
+            tma_load_3d(dst, &tm_k, &k_full[st], a * C::SW, key0, zk);
+        };
+        auto load_v = [&]() {
+          if (CHUNKED)
+            tma_load_4d(sV + st * C::V_TILE, &tm_v, &v_full[st], key0, 0, zk, chunk);
+          else
+            tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], key0, 0, zk);
+        };
         mbar_arrive_expect_tx(&k_full[st], C::K_TILE);
         for (int a = 0; a < C::DK / C::SW; ++a)
           SAGE_DCHECK(key0 < p.k_rows, kDbgTmaRow, key0, p.k_rows)
-          tma_load_3d(sK + st * C::K_TILE + a * C::BN * C::SW, &tm_k, &k_full[st], a * C::SW, key0, zk);
+          load_k(a);
         mbar_arrive_expect_tx(&v_full[st], C::V_TILE);
         // V^T is read along its key columns: a TMA column must start on 16 bytes
         SAGE_DCHECK((key0 & 15) == 0, kDbgTmaCol, key0, 2)
         SAGE_DCHECK(key0 < p.k_rows, kDbgTmaRow, key0, p.k_rows)
-        tma_load_3d(sV + st * C::V_TILE, &tm_v, &v_full[st], key0, 0, zk);
+        load_v();
         issued = j + 1;
       }
       if (!ok) {
@@ -594,6 +618,7 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
     const float qsr = __ldg(p.qs + q_off + min(q_row, Sq - 1));
     const float c = p.sm_log2e * qsr;
     const float* ksb = p.ks + ks_off;
+    int next_chunk = CHUNKED ? p.chunk_rows : INT_MAX;  // first key of the next chunk (chunked keys)
     const int last_key = CAUSAL ? q_row + off : 0x7fffffff;
     constexpr unsigned FULL = 0xffffffffu;
     float m = -INFINITY;
@@ -680,6 +705,11 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
       const uint32_t sph = QT >= 2 ? (j & 1) : ((j >> 1) & 1);
       const int kv0 = j * C::BN;
       float ksv[NB];
+      // chunked keys: when the next tile starts a new chunk, its scales lie ks_jump further on
+      if (CHUNKED && (j + 1) * C::BN >= next_chunk) {
+        ksb += p.ks_jump;
+        next_chunk += p.chunk_rows;
+      }
 #pragma unroll
       for (int i = 0; i < NB; ++i) {
         ksv[i] = ksn[i];
@@ -850,15 +880,38 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
   return true;
 }
 
-// One launch of sage_attn_kernel<D, CAUSAL, SINGLE> over CTAs [unit0, unit0 + n_units) of the plane-major
-// (plane, query group) order (all CTAs when n_units < 0).
-template <int D, bool CAUSAL, bool SINGLE>
+// 4-D uint8 tensor map: dims {x (contiguous), y, z, w}, box {bx, by, 1, 1}.
+static bool make_map4(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t w,
+                      uint64_t stride_y, uint64_t stride_z, uint64_t stride_w, uint32_t bx, uint32_t by,
+                      CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the CUDA driver");
+    return false;
+  }
+  cuuint64_t dims[4] = {x, y, z, w};
+  cuuint64_t strides[3] = {stride_y, stride_z, stride_w};
+  cuuint32_t box[4] = {bx, by, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
+// One launch of sage_attn_kernel<D, CAUSAL, SINGLE, CHUNKED> over CTAs [unit0, unit0 + n_units) of the
+// plane-major (plane, query group) order (all CTAs when n_units < 0).
+template <int D, bool CAUSAL, bool SINGLE, bool CHUNKED = false>
 static int launch_attention_part(const AttnArgs& a, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                                  AttnParams p, int unit0, int64_t n_units, cudaStream_t stream) {
   using C = AttnCfg<D, SINGLE>;
   p.q_groups = (a.Sq + C::QT * 128 - 1) / (C::QT * 128);
   p.unit0 = unit0;
-  auto kern = sage_attn_kernel<D, CAUSAL, SINGLE>;
+  auto kern = sage_attn_kernel<D, CAUSAL, SINGLE, CHUNKED>;
   if constexpr (C::REBALANCE) {
     // setmaxnreg moves registers between warpgroups inside the allocation the CTA was launched with; a
     // build allocating other than REGS_LAUNCH per thread would make the softmax's increase wait forever
@@ -922,16 +975,26 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   const bool varlen = a.cu_q != nullptr;
   // rows per (batch, head) plane of q8 and of k8 / v8t, and the number of planes
   const int64_t q_rows = varlen ? a.total_q : a.Sq;
-  const int64_t k_rows = varlen ? a.pad_total : kv_pad(a.Skv);
+  const bool chunked = !varlen && a.n_chunks > 0;
+  // chunked keys: k_rows is the rows of one chunk
+  const int64_t k_rows = varlen ? a.pad_total : (chunked ? a.chunk_rows : kv_pad(a.Skv));
   const uint64_t q_planes = varlen ? (uint64_t)a.H : (uint64_t)a.B * a.H;
   const uint64_t k_planes = varlen ? (uint64_t)a.Hkv : (uint64_t)a.B * a.Hkv;
   CUtensorMap mq, mk, mv;
   const CUtensorMapSwizzle qk_sw = C::SW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-  if (!make_map(&mq, a.q8, C::DK, q_rows, q_planes, C::DK, (uint64_t)q_rows * C::DK, C::SW, 128, qk_sw) ||
-      !make_map(&mk, a.k8, C::DK, k_rows, k_planes, C::DK, (uint64_t)k_rows * C::DK, C::SW, C::BN, qk_sw) ||
-      !make_map(&mv, a.v8t, k_rows, D, k_planes, k_rows, (uint64_t)k_rows * D, C::BN, D,
-                C::VSW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+  const CUtensorMapSwizzle v_sw = C::VSW == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  if (!make_map(&mq, a.q8, C::DK, q_rows, q_planes, C::DK, (uint64_t)q_rows * C::DK, C::SW, 128, qk_sw))
     return kStatusInvalid;
+  if (chunked) {
+    const uint64_t kc = (uint64_t)k_rows * C::DK, vc = (uint64_t)k_rows * D;  // bytes of one plane's chunk
+    if (!make_map4(&mk, a.k8, C::DK, k_rows, k_planes, a.n_chunks, C::DK, kc, kc * k_planes, C::SW, C::BN,
+                   qk_sw) ||
+        !make_map4(&mv, a.v8t, k_rows, D, k_planes, a.n_chunks, k_rows, vc, vc * k_planes, C::BN, D, v_sw))
+      return kStatusInvalid;
+  } else if (!make_map(&mk, a.k8, C::DK, k_rows, k_planes, C::DK, (uint64_t)k_rows * C::DK, C::SW, C::BN, qk_sw) ||
+             !make_map(&mv, a.v8t, k_rows, D, k_planes, k_rows, (uint64_t)k_rows * D, C::BN, D, v_sw)) {
+    return kStatusInvalid;
+  }
   AttnParams p;
   p.qs = a.qs;
   p.ks = a.ks;
@@ -948,7 +1011,11 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   p.Sq = a.Sq;
   p.Skv = a.Skv;
   p.row0 = a.row0 == INT_MIN ? a.Skv - a.Sq : a.row0;
-  p.nkb = varlen ? 0 : (int)(k_rows / kKvBlock);
+  p.nkb = varlen ? 0 : (int)(kv_pad(a.Skv) / kKvBlock);  // K-scale blocks holding keys
+  p.n_chunks = chunked ? a.n_chunks : 0;
+  p.chunk_rows = chunked ? a.chunk_rows : 0;
+  p.ks_plane = chunked ? a.chunk_rows / kKvBlock : p.nkb;
+  p.ks_jump = chunked ? (int64_t)(k_planes - 1) * (a.chunk_rows / kKvBlock) : 0;
   p.cu_q = a.cu_q;
   p.cu_k = a.cu_k;
   p.cu_pad = a.cu_pad;
@@ -974,6 +1041,7 @@ static int launch_attention_t(const AttnArgs& a, cudaStream_t stream) {
   }
   p.sm_log2e = (float)(1.0 / std::sqrt((double)D) * 1.4426950408889634);
   p.out_f16 = a.out_dtype == 1;
+  if (chunked) return launch_attention_part<D, CAUSAL, false, true>(a, mq, mk, mv, p, 0, -1, stream);
   if constexpr (C::QT == 2 && !CAUSAL) {
     int64_t main_ctas = 0;
     if (attention_tail_split(D, 0, varlen, q_planes, a.Sq, device_sms(), &main_ctas)) {

@@ -258,22 +258,29 @@ int sage_attn_fwd(const int8_t* q8, const float* qs, const int8_t* k8, const flo
   return launch_attention(a, static_cast<cudaStream_t>(stream));
 }
 
-int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
-                       const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
-                       int causal, int q_row0, int64_t osb, int64_t oss, int64_t osh, float* lse, int* status,
-                       void* stream) {
-  if (q_row0 < 0 || (int64_t)q_row0 + Sq > (int64_t)Skv) {
-    g_error[0] = 0;
-    set_error("query rows %d..%d lie outside the %d keys", q_row0, q_row0 + Sq - 1, Skv);
-    return SAGE_ERR_INVALID;
-  }
-  NvtxRange nvtx("sage_attn_fwd_rows");
+// sage_attn_fwd_rows / sage_attn_fwd_chunked: query rows placed at q_row0 among the keys, keys optionally in
+// chunks (n_chunks > 0).
+static int attn_fwd_placed(const char* name, const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+                           const uint8_t* v8t, const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq,
+                           int Skv, int D, int causal, int q_row0, int chunk_rows, int n_chunks, int64_t osb,
+                           int64_t oss, int64_t osh, float* lse, int* status, void* stream) {
+  NvtxRange nvtx(name);
   g_error[0] = 0;
   int rc = check_common(out_dtype, B, Sq, H, D);
   if (rc != SAGE_OK) return rc;
   if (Hkv <= 0 || H % Hkv != 0 || Skv <= 0) {
     set_error("heads %d must be a multiple of kv heads %d and kv length %d positive", H, Hkv, Skv);
     return SAGE_ERR_UNSUPPORTED;
+  }
+  if (q_row0 < 0 || (int64_t)q_row0 + Sq > (int64_t)Skv) {
+    set_error("query rows %d..%d lie outside the %d keys", q_row0, q_row0 + Sq - 1, Skv);
+    return SAGE_ERR_INVALID;
+  }
+  if (n_chunks < 0 || (n_chunks > 0 && (chunk_rows <= 0 || chunk_rows % 128 != 0 ||
+                                        (int64_t)chunk_rows * n_chunks < (int64_t)Skv))) {
+    set_error("%d chunks of %d keys: chunks must be positive multiples of 128 keys covering the %d keys", n_chunks,
+              chunk_rows, Skv);
+    return SAGE_ERR_INVALID;
   }
   if (!aligned16(q8) || !aligned16(k8) || !aligned16(v8t) || qs == nullptr || ks == nullptr || vs == nullptr) {
     set_error("quantised operands must be 16-byte aligned and non-null");
@@ -284,7 +291,30 @@ int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, cons
   AttnArgs a{q8, qs, k8, ks, v8t, vs, out, out_dtype, Strides3{osb, oss, osh}, lse, status, B, H, Hkv, Sq, Skv, D,
              causal ? 1 : 0};
   a.row0 = q_row0;
+  a.chunk_rows = n_chunks > 0 ? chunk_rows : 0;
+  a.n_chunks = n_chunks;
   return launch_attention(a, static_cast<cudaStream_t>(stream));
+}
+
+int sage_attn_fwd_rows(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                       const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
+                       int causal, int q_row0, int64_t osb, int64_t oss, int64_t osh, float* lse, int* status,
+                       void* stream) {
+  return attn_fwd_placed("sage_attn_fwd_rows", q8, qs, k8, ks, v8t, vs, out, out_dtype, B, H, Hkv, Sq, Skv, D, causal,
+                         q_row0, 0, 0, osb, oss, osh, lse, status, stream);
+}
+
+int sage_attn_fwd_chunked(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks, const uint8_t* v8t,
+                          const float* vs, void* out, int out_dtype, int B, int H, int Hkv, int Sq, int Skv, int D,
+                          int causal, int q_row0, int chunk_rows, int n_chunks, int64_t osb, int64_t oss, int64_t osh,
+                          float* lse, int* status, void* stream) {
+  if (n_chunks <= 0) {
+    g_error[0] = 0;
+    set_error("sage_attn_fwd_chunked needs at least one chunk");
+    return SAGE_ERR_INVALID;
+  }
+  return attn_fwd_placed("sage_attn_fwd_chunked", q8, qs, k8, ks, v8t, vs, out, out_dtype, B, H, Hkv, Sq, Skv, D,
+                         causal, q_row0, chunk_rows, n_chunks, osb, oss, osh, lse, status, stream);
 }
 
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D) {

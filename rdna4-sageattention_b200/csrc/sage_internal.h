@@ -103,6 +103,11 @@ struct AttnArgs {
   int64_t pad_total = 0;
   // dense: position of query row 0 in the key sequence (causal keeps key j <= row0 + i); INT_MIN: Skv - Sq
   int row0 = INT_MIN;
+  // dense, chunked keys (n_chunks > 0): k8 [n_chunks, B, Hkv, chunk_rows, DK], ks [n_chunks, B, Hkv,
+  // chunk_rows / 32], v8t [n_chunks, B, Hkv, D, chunk_rows]; key j is row j % chunk_rows of chunk
+  // j / chunk_rows (chunk_rows a multiple of 128)
+  int chunk_rows = 0;
+  int n_chunks = 0;
 };
 int launch_attention(const AttnArgs& a, cudaStream_t stream);
 // Query rows one attention CTA owns for head dim D (the grid is B * H * ceil(Sq / rows)).

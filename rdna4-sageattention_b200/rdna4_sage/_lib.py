@@ -47,6 +47,8 @@ SIGNATURES = {
                              _c_i, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
     "sage_attn_fwd_rows": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i,
                                   _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
+    "sage_attn_fwd_chunked": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i,
+                                     _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
     "sage_workspace_bytes": (_c_sz, [_c_i, _c_i, _c_i, _c_i, _c_i, _c_i]),
     "sage_attention": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64,
                               _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p, _c_i64, _c_i64,

@@ -3,10 +3,12 @@
 Steps per call (all ranks of `group`, same order):
   1. V channel amax of the local chunk, then an all-reduce (MAX) so every rank quantises V with the same
      per-channel scale as a single-GPU call would;
-  2. local Q quantisation, local K+V quantisation with the global amax (chunks start at multiples of 32
-     tokens, so every 32-key K scale block lies inside one chunk and equals the single-GPU one);
+  2. local Q quantisation, local K+V quantisation with the global amax straight into the buffers the
+     all-gather sends (chunks are multiples of 128 tokens, so every 32-key K scale block lies inside one
+     chunk and equals the single-GPU one, and no 128-key tile of the kernel straddles two chunks);
   3. all-gather of the quantised K (int8), its block scales and V^T (e4m3) - 1 byte per element instead of
-     the 2-byte inputs - and reassembly into the kernel's [B, Hkv, S, DK] / [B, Hkv, D, S] layouts;
+     the 2-byte inputs - into [world, B, Hkv, chunk, ...] buffers, which the kernel reads as they are
+     (sage_attn_fwd_chunked: key j is row j % chunk of chunk j / chunk), so nothing is re-laid out;
   4. the attention kernel on the local query rows against all keys; causal calls give the kernel the
      chunk's first row position, so row i keeps keys j <= start + i, as in the single-GPU call.
 The output rows of each rank equal the corresponding rows of the single-GPU call bit for bit.  (With
@@ -23,12 +25,18 @@ import torch.distributed as dist
 from . import _attention, _lib
 
 KV_BLOCK = _attention.KV_BLOCK
+CHUNK_ALIGN = 128  # tokens: the kernel's key tile
 
 
-def chunk_bounds(S: int, world: int, rank: int, align: int = KV_BLOCK) -> tuple[int, int]:
-    """[start, end) of rank's token chunk: equal chunks rounded up to `align`, the last one shorter."""
+def chunk_rows(S: int, world: int, align: int = CHUNK_ALIGN) -> int:
+    """Tokens per chunk: S split into `world` equal parts, rounded up to `align`."""
     per = (S + world - 1) // world
-    per = (per + align - 1) // align * align
+    return max(align, (per + align - 1) // align * align)
+
+
+def chunk_bounds(S: int, world: int, rank: int, align: int = CHUNK_ALIGN) -> tuple[int, int]:
+    """[start, end) of rank's token chunk: equal chunks rounded up to `align`, the last one shorter."""
+    per = chunk_rows(S, world, align)
     start = min(rank * per, S)
     return start, min(start + per, S)
 
@@ -69,6 +77,17 @@ class KernelBackend:
                                              _attention.status_word(out.device).data_ptr(), self.stream),
                    "sage_attn_fwd_rows")
 
+    def attn_chunked(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D, causal, q_row0):
+        """k8 [n, B, Hkv, chunk, DK], ks [n, B, Hkv, chunk / 32], v8t [n, B, Hkv, D, chunk]."""
+        B = out.shape[0]
+        n, chunk = k8.shape[0], k8.shape[3]
+        _lib.check(self.L.sage_attn_fwd_chunked(q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(),
+                                                v8t.data_ptr(), vs.data_ptr(), out.data_ptr(),
+                                                _attention.DTYPES[out.dtype], B, H, Hkv, Sq, Skv, D, int(causal),
+                                                int(q_row0), chunk, n, *out.stride()[:3], None,
+                                                _attention.status_word(out.device).data_ptr(), self.stream),
+                   "sage_attn_fwd_chunked")
+
 
 def _gather(x: torch.Tensor, world: int, group) -> torch.Tensor:
     """[world, *x.shape]: every rank's x, in rank order (NCCL writes straight into one buffer)."""
@@ -97,50 +116,48 @@ def attention_cp(q, k, v, total_len: int, group=None, sm_scale=None, backend=Non
         raise ValueError(f"rank {rank}: expected a chunk of {end - start} tokens, got q {Sr}, k {k.shape[1]}")
     be = backend if backend is not None else KernelBackend(q.device)
     dev = q.device
-    per = chunk_bounds(total_len, world, 0)[1]          # padded chunk length (a multiple of 32)
+    per = chunk_rows(total_len, world)                  # rows of every chunk buffer (a multiple of 128)
     dk = be.qk_row_bytes(D)
     # 1. global V channel amax
     vs = torch.zeros((B, Hkv, D), device=dev, dtype=torch.float32)
     if Sr > 0:
         be.v_amax(v, vs)
     dist.all_reduce(vs, op=dist.ReduceOp.MAX, group=group)
-    # 2. local quantisation; every rank's K chunk is quantised to `per` rows (zero rows past its end)
+    # 2. local quantisation, K and V straight into the buffers the all-gather sends: `per` rows each (a
+    # multiple of 128, so a full chunk's padded length is `per` itself); a shorter last chunk goes through
+    # its own padded buffers, and rows past its end are zero (their keys are masked, but V^T bytes must be
+    # finite e4m3)
     fold = float(_attention.sm_fold(sm_scale, D))
     q8 = torch.empty((B, H, Sr, dk), device=dev, dtype=torch.int8)
     qs = torch.empty((B, H, Sr), device=dev, dtype=torch.float32)
     if Sr > 0:
         be.quant_q(q, fold, q8, qs)
-    k8 = torch.zeros((B, Hkv, per, dk), device=dev, dtype=torch.int8)
-    ks = torch.zeros((B, Hkv, per // KV_BLOCK), device=dev, dtype=torch.float32)
-    v8t = torch.zeros((B, Hkv, D, per), device=dev, dtype=torch.uint8)
-    if Sr > 0:
-        spad = (Sr + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
-        k8_l = torch.empty((B, Hkv, spad, dk), device=dev, dtype=torch.int8)
-        ks_l = torch.empty((B, Hkv, spad // KV_BLOCK), device=dev, dtype=torch.float32)
-        v8t_l = torch.empty((B, Hkv, D, spad), device=dev, dtype=torch.uint8)
-        be.quant_kv(k, v, vs, k8_l, ks_l, v8t_l)
-        k8[:, :, :spad] = k8_l
-        ks[:, :, :spad // KV_BLOCK] = ks_l
-        v8t[..., :spad] = v8t_l
-    # 3. all-gather the quantised keys and values, then reassemble [B, Hkv, world*per, ...]
+    if Sr == per:
+        k8 = torch.empty((B, Hkv, per, dk), device=dev, dtype=torch.int8)
+        ks = torch.empty((B, Hkv, per // KV_BLOCK), device=dev, dtype=torch.float32)
+        v8t = torch.empty((B, Hkv, D, per), device=dev, dtype=torch.uint8)
+        be.quant_kv(k, v, vs, k8, ks, v8t)
+    else:
+        k8 = torch.zeros((B, Hkv, per, dk), device=dev, dtype=torch.int8)
+        ks = torch.zeros((B, Hkv, per // KV_BLOCK), device=dev, dtype=torch.float32)
+        v8t = torch.zeros((B, Hkv, D, per), device=dev, dtype=torch.uint8)
+        if Sr > 0:
+            spad = (Sr + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
+            k8_l = torch.empty((B, Hkv, spad, dk), device=dev, dtype=torch.int8)
+            ks_l = torch.empty((B, Hkv, spad // KV_BLOCK), device=dev, dtype=torch.float32)
+            v8t_l = torch.empty((B, Hkv, D, spad), device=dev, dtype=torch.uint8)
+            be.quant_kv(k, v, vs, k8_l, ks_l, v8t_l)
+            k8[:, :, :spad] = k8_l
+            ks[:, :, :spad // KV_BLOCK] = ks_l
+            v8t[..., :spad] = v8t_l
+    # 3. all-gather into [world, B, Hkv, per, ...]: the chunked layout the kernel reads
     g_k8 = _gather(k8, world, group)
     g_ks = _gather(ks, world, group)
     g_v8 = _gather(v8t, world, group)
-    spad_total = world * per
-    k8_full = g_k8.permute(1, 2, 0, 3, 4).reshape(B, Hkv, spad_total, dk)
-    ks_full = g_ks.permute(1, 2, 0, 3).reshape(B, Hkv, spad_total // KV_BLOCK)
-    v8t_full = g_v8.permute(1, 2, 3, 0, 4).reshape(B, Hkv, D, spad_total)
-    # keys past total_len are zero in every chunk; the kernel masks keys >= total_len.  Trim the padded
-    # tail to the single-GPU padded length so the layouts match it exactly.
-    spad_exact = (total_len + KV_BLOCK - 1) // KV_BLOCK * KV_BLOCK
-    k8_full = k8_full[:, :, :spad_exact].contiguous()
-    ks_full = ks_full[:, :, :spad_exact // KV_BLOCK].contiguous()
-    v8t_full = v8t_full[..., :spad_exact].contiguous()
     # 4. local rows against all keys
     out = torch.empty((B, Sr, H, D), device=dev, dtype=q.dtype)
     if Sr > 0:
-        be.attn(q8, qs, k8_full, ks_full, v8t_full, vs, out, H, Hkv, Sr, total_len, D, causal=bool(is_causal),
-                q_row0=start)
+        be.attn_chunked(q8, qs, g_k8, g_ks, g_v8, vs, out, H, Hkv, Sr, total_len, D, bool(is_causal), start)
     return out
 
 
@@ -155,4 +172,4 @@ def ops_per_rank(B, H, Sr, S, D) -> float:
     return 4.0 * B * H * Sr * S * D
 
 
-__all__ = ["attention_cp", "chunk_bounds", "shard", "KernelBackend", "ops_per_rank"]
+__all__ = ["attention_cp", "chunk_bounds", "chunk_rows", "shard", "KernelBackend", "ops_per_rank"]

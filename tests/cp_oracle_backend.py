@@ -44,3 +44,11 @@ class OracleBackend:
                                         causal, block_n=32, row0=q_row0)
                 res[b, :, h] = o
         out.copy_(torch.from_numpy(res).to(out.dtype))
+
+    def attn_chunked(self, q8, qs, k8, ks, v8t, vs, out, H, Hkv, Sq, Skv, D, causal, q_row0):
+        # the chunked layout reassembled to the plain one ([n, B, Hkv, chunk, ...] -> [B, Hkv, n * chunk, ...])
+        n, B, _, chunk = k8.shape[:4]
+        k8f = k8.permute(1, 2, 0, 3, 4).reshape(B, Hkv, n * chunk, -1)
+        ksf = ks.permute(1, 2, 0, 3).reshape(B, Hkv, -1)
+        v8f = v8t.permute(1, 2, 3, 0, 4).reshape(B, Hkv, D, n * chunk)
+        self.attn(q8, qs, k8f, ksf, v8f, vs, out, H, Hkv, Sq, Skv, D, causal=causal, q_row0=q_row0)

@@ -1,4 +1,4 @@
-"""Context-parallel host logic (rdna4_sage.cp) on CPU: two gloo ranks each hold a 32-aligned token chunk;
+"""Context-parallel host logic (rdna4_sage.cp) on CPU: two gloo ranks each hold a 128-aligned token chunk;
 with the oracle standing in for the kernels, the gathered result equals the unsharded call bit for bit."""
 import os
 import sys
@@ -64,7 +64,7 @@ def test_cp_two_ranks_equal_single_call(S, H, Hkv, D, sm_scale, causal):
     be.attn(q8, qs, k8, ks, v8t, vs, ref, H, Hkv, S, S, D, causal=causal, q_row0=0)
     got = np.concatenate([results[r] for r in range(world)], axis=1)
     np.testing.assert_array_equal(got, ref.float().numpy())
-    assert cp.chunk_bounds(S, world, 0)[1] % 32 == 0
+    assert cp.chunk_bounds(S, world, 0)[1] % 128 == 0
 
 
 def test_chunk_bounds_cover_sequence():
@@ -74,8 +74,8 @@ def test_chunk_bounds_cover_sequence():
         assert spans[0][0] == 0 and spans[-1][1] == S
         for (a, b), (c, d) in zip(spans, spans[1:]):
             assert b == c
-            if d > c:                       # a chunk followed by a non-empty one is 32-aligned
-                assert (b - a) % 32 == 0
+            if d > c:                       # a chunk followed by a non-empty one is 128-aligned
+                assert (b - a) % 128 == 0
 
 
 def _failing_worker(rank, world, port, results):

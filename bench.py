@@ -321,6 +321,17 @@ def run_hunyuan_cp(args):
         dist.destroy_process_group()
 
 
+def launches_per_call(b, heads, n, d, nsm):
+    """Kernels one dense non-causal sage_attention call launches (this library's own): the V amax, Q, K and V
+    quantisers for kv lengths above 6144 (D 128 / 256; one single-launch quantiser otherwise), and the
+    attention kernel, plus the single-tile launch that finishes a last wave at most half full (D 96 / 128)."""
+    quant = 1 if (n <= 6144 and d <= 128) else (4 if d in (128, 256) else 3)
+    pairs = b * heads * ((n + 255) // 256)
+    full, rest = divmod(pairs, nsm)
+    tail = 1 if d in (96, 128) and full > 0 and rest > 0 and 2 * rest <= nsm else 0
+    return quant + 1 + tail
+
+
 def run_ours(args):
     _our_paths()
     import rdna4_sage
@@ -506,7 +517,8 @@ def run_ours(args):
              "api": f"rdna4_sage.attention_host (sage_attention_host), {hpc} heads per chunk, copies overlapped",
              "device_api": {"value": total_ops / (ms_e2e_dev * 1e-3) / 1e12, "ms_per_step": ms_e2e_dev,
                             "api": "copy in + sageattention.sageattn + copy out, unpipelined"}},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": launches_per_call(Bq, Hq, Sq, Dq, torch.cuda.get_device_properties(dev).multi_processor_count)
+                            * args.steps,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tops, "unit": "TOPS",
                          "frac": achieved / peak_tops, "traffic": traffic,
                          "kernel": "sage_attn_kernel<128,false>", "ms_per_launch": attn_ms,

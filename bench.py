@@ -35,7 +35,7 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "rdna4-sageattention_b200")
-# The reference installed offline (pip --target baseline/_ref /root/reference): it ships packages named
+# The reference installed offline (pip install --target baseline/_ref of its source tree): it ships packages named
 # like this repo's (sageattention, rdna4_sage), so the reference arm runs in a process that imports only it.
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 

@@ -82,6 +82,23 @@ def test_argument_errors_without_gpu():
     assert rc == _lib.SAGE_ERR_UNSUPPORTED      # 3 heads over 2 kv heads
 
 
+def test_placed_and_chunked_attention_arguments_without_gpu():
+    # sage_attn_fwd_rows / sage_attn_fwd_chunked reject a row block outside the keys and chunk geometry that
+    # a key tile could straddle, on the host, before any launch
+    L = _lib.lib()
+    p = 256
+    # q8 qs k8 ks v8t vs out, out_dtype, B H Hkv Sq Skv D, causal, q_row0, strides, lse, status, stream
+    head = [p] * 7 + [0, 1, 2, 2, 100, 1000, 128, 1]
+    tail = [256, 256, 256, None, None, None]
+    assert L.sage_attn_fwd_rows(*head, 901, *tail) == _lib.SAGE_ERR_INVALID        # rows 901..1000 > keys
+    assert b"outside" in L.sage_last_error()
+    assert L.sage_attn_fwd_rows(*head, -1, *tail) == _lib.SAGE_ERR_INVALID
+    assert L.sage_attn_fwd_chunked(*head, 0, 200, 8, *tail) == _lib.SAGE_ERR_INVALID   # 200 not a multiple of 128
+    assert b"multiples of 128" in L.sage_last_error()
+    assert L.sage_attn_fwd_chunked(*head, 0, 256, 3, *tail) == _lib.SAGE_ERR_INVALID   # 768 keys < 1000
+    assert L.sage_attn_fwd_chunked(*head, 0, 256, 0, *tail) == _lib.SAGE_ERR_INVALID   # no chunk
+
+
 def test_host_pipeline_planner_without_gpu():
     """sage_attention_host's chunking and workspace are host arithmetic (148 SMs assumed without a GPU)."""
     L = _lib.lib()

@@ -313,7 +313,7 @@ __global__ void __launch_bounds__(kRows) quant_q_pair_kernel(const T* __restrict
 // ------------------------------------------------------------------------------------------------
 // K + V: one thread per key row; a warp is one 32-key K scale block
 // ------------------------------------------------------------------------------------------------
-template <int D, typename T, bool VARLEN>
+template <int D, typename T, bool VARLEN, bool WITH_V = true>
 __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, int S,
                                                          int H, Strides3 sk, Strides3 sv, const float* __restrict__ vs,
                                                          int8_t* __restrict__ k8, float* __restrict__ ks,
@@ -349,8 +349,11 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
   }
   const int spad = (S + kKvBlock - 1) / kKvBlock * kKvBlock;
   __shared__ float fac[D];   // per-channel V factor 448 / max(amax, 1e-30) (sage_quant.py:68-69)
-  for (int c = threadIdx.x; c < D; c += blockDim.x) fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
-  __syncthreads();
+  if (WITH_V) {
+    for (int c = threadIdx.x; c < D; c += blockDim.x)
+      fac[c] = __fdiv_rn(448.0f, fmaxf(vs[(int64_t)bh * D + c], 1e-30f));
+    __syncthreads();
+  }
   if (s - (int)(threadIdx.x & 31) >= spad) return;   // whole warp past the padded length
   const bool valid = s < S;        // real key (rows in [S, spad) are zero padding)
   const bool inpad = s < spad;     // row exists in the padded tensors
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(kRows) quant_kv_kernel(const T* __restrict__ k
   quant_k_row<D, T>(krow, valid, inpad, k8 + orow * DK, ks + orow / kKvBlock, lane);
 
   // V: per-channel scale to e4m3
-  if (!inpad) return;
+  if (!WITH_V || !inpad) return;
   const T* vrow = v + src_b * sv.b + (t0 + (valid ? s : 0)) * sv.s + (int64_t)h * sv.h;
   quant_v_row<D, T>(vrow, valid, fac, v8t + vbase + s, pitch);
 }
@@ -422,7 +425,7 @@ __global__ void __launch_bounds__(kRows) quant_kv_pair_kernel(const T* __restric
 }
 
 // ------------------------------------------------------------------------------------------------
-// V alone (dense calls with D = 128 and 256, beside the K-only pair kernel): a CTA converts 128 keys of one
+// V alone (dense calls, beside the K-only kernels): a CTA converts 128 keys of one
 // (batch, kv head) to e4m3 with the channel factors and writes them transposed.  Loads are coalesced along
 // the key rows (16 lanes per 256-byte row for D = 128); the codes go through a shared-memory tile in which
 // channel c's keys are contiguous (16-byte chunks XOR-swizzled by c / 8, so the 16 lanes of one row hit 8
@@ -825,10 +828,15 @@ static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides
       }
     }
     dim3 grid((spad + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
-    if (sg.cu != nullptr)
+    if (sg.cu != nullptr) {
       quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
-    else
-      quant_kv_kernel<D, T, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
+    } else {
+      // dense D = 64 / 96: K in the one-thread kernel, V in its own
+      quant_kv_kernel<D, T, false, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
+      if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
+      dim3 grid3((spad + 127) / 128, min(kMaxGridY, B * H - bh0));
+      quant_v_tile_kernel<D, T><<<grid3, 256, 0, stream>>>(vp, S, H, sv, vs, v8t, bh0);
+    }
     if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
   }
   return kStatusOk;

@@ -323,9 +323,9 @@ def run_hunyuan_cp(args):
 
 def launches_per_call(b, heads, n, d, nsm):
     """Kernels one dense non-causal sage_attention call launches (this library's own): the V amax, Q, K and V
-    quantisers for kv lengths above 6144 (D 128 / 256; one single-launch quantiser otherwise), and the
+    quantisers (one single-launch quantiser instead for kv lengths up to 6144 with D <= 128), and the
     attention kernel, plus the single-tile launch that finishes a last wave at most half full (D 96 / 128)."""
-    quant = 1 if (n <= 6144 and d <= 128) else (4 if d in (128, 256) else 3)
+    quant = 1 if (n <= 6144 and d <= 128) else 4
     pairs = b * heads * ((n + 255) // 256)
     full, rest = divmod(pairs, nsm)
     tail = 1 if d in (96, 128) and full > 0 and rest > 0 and 2 * rest <= nsm else 0

@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--weak]
 
 One step = one call of the quantised path that sageattention.sageattn runs when it takes a call
-(rdna4_sage.attention: V amax, Q quantiser, K+V quantiser, int8/fp8 attention) on
+(rdna4_sage.attention: V amax, Q, K and V quantisers, int8/fp8 attention) on
 B=1, H=40, N=32760, D=128, bf16, NHD, K ~ N(0,1) + per-channel offset N(0, std 2).  Inputs (1.0 GB) are
 larger than the 126 MB L2, so consecutive steps do not hit in L2.
 

@@ -780,11 +780,15 @@ __global__ void __launch_bounds__(AttnCfg<D, SINGLE>::THREADS, 1)
       for (int i = 0; i < NB; ++i) kp[i] = kb[i];
     }
     // ---------------------------------------------------------------- epilogue
-    // A parity wait must not run two phases ahead of its barrier.  With QT >= 2 the last S was issued
-    // after the previous tile's P.V, so that one has landed; with QT = 1 it was issued before it, so the
-    // previous tile's P.V is awaited first.
-    if (ok && QT == 1 && n_tiles > 1) ok = wait_s(&o_done[t], (n_tiles - 2) & 1);
-    if (ok && n_tiles > 0) ok = wait_s(&o_done[t], (n_tiles - 1) & 1);
+    // A parity wait must neither run ahead of its barrier nor fall two phases behind it.  With QT >= 2 the
+    // last S was issued after the previous tile's P.V, so that one has landed and o_done is one phase from
+    // the last.  With QT = 1 the last S was issued before the previous tile's P.V, and once P is announced
+    // both of the last two P.Vs may land before this warp polls (a warp slowed by other CTAs on the SM), so
+    // no parity of o_done is safe: the warp waits for mma_drain instead, committed once after the MMA
+    // thread's last MMA (also when it left its loop on an error, hence the abort test).  Both waits serve
+    // the last tile's splits meanwhile.
+    if (ok && n_tiles > 0)
+      ok = QT == 1 ? wait_s(mma_drain, 0) && !__any_sync(FULL, aborted(wc)) : wait_s(&o_done[t], (n_tiles - 1) & 1);
     if (ok) {
       tc_fence_after();
       // a row with no keys (an empty varlen key sequence) gets zeros

@@ -161,9 +161,12 @@ int sage_attention_varlen(const void* q, const void* k, const void* v, int dtype
 
 /* sage_attention on tensors in HOST memory (pinned for overlap; strides as above, channel axis contiguous,
  * no alignment rule for the host pointers): q, k, v, out and lse (nullable, [B, H, Sq]) are host
- * pointers.  The heads are cut into chunks of `heads_per_chunk` query heads (a multiple of H / Hkv;
- * 0 = chosen by the library); each chunk is copied in on a library-owned stream, attended on `stream`
- * and copied out on a second library stream, so copies and kernels of neighbouring chunks overlap.
+ * pointers.  The heads are cut into chunks of at most `heads_per_chunk` query heads (a multiple of
+ * H / Hkv; 0 = chosen by the library, and sage_host_heads_per_chunk returns the choice); the library may
+ * make the first and last chunks smaller (halving towards one group of H / Hkv heads) where its model of
+ * the pipeline says that fills or drains it sooner.  Each chunk is copied in on a library-owned stream,
+ * attended on `stream` and copied out on a second library stream, so copies and kernels of neighbouring
+ * chunks overlap.  The chunking does not change the result: every head is computed on its own.
  * When the work on `stream` completes, `out` and `lse` hold the result.  `workspace` is device memory
  * of sage_host_workspace_bytes(...) bytes (256-byte aligned) for two chunks in flight plus the quantised
  * tensors.  The reference has no such entry (its callers copy to the GPU themselves and call

@@ -113,7 +113,8 @@ def test_host_pipeline_planner_without_gpu():
     assert L.sage_host_heads_per_chunk(1, 32, 8, 4096, 4096, 128, 64) == 32        # clamped to H
     a256 = lambda n: (n + 255) // 256 * 256
     slot = 2 * a256(B * S * 8 * D * 2) + 2 * a256(B * S * 8 * D * 2) + a256(B * 8 * S * 4)
-    assert L.sage_host_workspace_bytes(B, H, Hkv, S, S, D, 8) == 2 * slot + a256(
+    # two staging slots and the quantised-tensor scratch of each (the slots' chunks run on two streams)
+    assert L.sage_host_workspace_bytes(B, H, Hkv, S, S, D, 8) == 2 * slot + 2 * a256(
         L.sage_workspace_bytes(B, 8, 8, S, S, D))
     rc = L.sage_attention_host(None, None, None, 0, B, H, Hkv, S, S, D, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.0, 0, None, 0, 0,
                                0, None, 0, None, 0, None, None)

@@ -78,3 +78,20 @@ def test_host_rejects():
     L = _lib.lib()
     assert L.sage_host_heads_per_chunk(1, 6, 3, 128, 128, 128, 0) % 2 == 0
     assert L.sage_host_workspace_bytes(1, 6, 4, 128, 128, 128, 0) == 0    # H not a multiple of Hkv
+
+
+@pytest.mark.parametrize("D,S,H,hpc", [(128, 32760, 12, 6), (256, 8192, 8, 2)])
+def test_overlapped_chunks_with_one_tile_ctas(D, S, H, hpc):
+    """Neighbouring chunks run on two streams, so the CTAs of one chunk's kernels share SMs with the next
+    chunk's quantisers.  A one-tile CTA (the tail launch of a 6-head D = 128 chunk; every D = 256 CTA)
+    leaves room on its SM for them, and a softmax warp slowed that way between announcing its last P and
+    its epilogue used to find the per-tile P.V barrier two phases on and wait out its 2 s limit.  Each
+    call must finish with a clean status and the device call's exact result."""
+    q, k, v = _inputs("NHD", 1, H, H, S, S, D, torch.bfloat16)
+    ro, _ = _device_ref(q, k, v, "NHD", False)
+    out = torch.empty((1, S, H, D), dtype=torch.bfloat16).pin_memory()
+    for _ in range(4):
+        out.fill_(float("nan"))
+        o = rdna4_sage.attention_host(q, k, v, "NHD", heads_per_chunk=hpc, out=out)
+        _attention.check_status()
+        assert torch.equal(o, ro)

@@ -348,7 +348,8 @@ def _bsh_host(t: torch.Tensor, layout: str):
 def attention_host(q, k, v, layout="HND", sm_scale=None, is_causal=False, return_lse=False, device=None,
                    heads_per_chunk=0, out=None, non_blocking=False, devices=None):
     """attention() for q, k, v in host memory, with the copies to and from the GPU overlapped with the
-    kernels (chunks of heads: copy in / attend / copy out on three streams, one C-ABI call).
+    kernels (chunks of heads: copy in on one stream, attend on two alternating streams, copy out on a fourth;
+    one C-ABI call).
 
     q, k, v: CPU tensors (pinned memory for the copies to overlap), shapes as for attention().  Returns
     the result in q's layout, a view of a pinned CPU (B, Sq, H, D) buffer (or of `out`, a CPU tensor of

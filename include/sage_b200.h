@@ -172,6 +172,10 @@ int sage_attention_varlen(const void* q, const void* k, const void* v, int dtype
  * tensors.  The reference has no such entry (its callers copy to the GPU themselves and call
  * attention(), _attention.py:97); this one replaces that copy + attention() + copy-back sequence. */
 int sage_host_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk);
+/* The chunk sizes (query heads, in order) sage_attention_host uses for these arguments: returns their count
+ * (0 for unsupported arguments) and writes the first max_chunks of them to `sizes` (nullable). */
+int sage_host_chunk_plan(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk, int* sizes,
+                         int max_chunks);
 size_t sage_host_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk);
 int sage_attention_host(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq,
                         int Skv, int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh,

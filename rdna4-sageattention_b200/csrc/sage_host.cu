@@ -235,6 +235,17 @@ int sage_host_heads_per_chunk(int B, int H, int Hkv, int Sq, int Skv, int D, int
   return plan_chunks(B, H, Hkv, Sq, Skv, D, heads_per_chunk, nullptr);
 }
 
+int sage_host_chunk_plan(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk, int* sizes,
+                         int max_chunks) {
+  const int hg = sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
+  if (hg == 0) return 0;
+  std::vector<int> plan;
+  plan_chunks(B, H, Hkv, Sq, Skv, D, hg, &plan);
+  if (sizes != nullptr)
+    for (int i = 0; i < (int)plan.size() && i < max_chunks; ++i) sizes[i] = plan[i];
+  return (int)plan.size();
+}
+
 size_t sage_host_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D, int heads_per_chunk) {
   const int hg = sage_host_heads_per_chunk(B, H, Hkv, Sq, Skv, D, heads_per_chunk);
   if (hg == 0) return 0;

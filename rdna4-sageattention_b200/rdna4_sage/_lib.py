@@ -61,6 +61,7 @@ SIGNATURES = {
                                      _c_i, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p, _c_i64,
                                      _c_i64, _c_p, _c_p, _c_sz, _c_p, _c_p]),
     "sage_host_heads_per_chunk": (_c_i, [_c_i] * 7),
+    "sage_host_chunk_plan": (_c_i, [_c_i] * 7 + [_c_p, _c_i]),
     "sage_host_workspace_bytes": (_c_sz, [_c_i] * 7),
     "sage_attention_host": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64,
                                    _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_d, _c_i, _c_p,

@@ -136,3 +136,26 @@ def test_varlen_workspace_and_argument_checks_without_gpu():
     rc = L.sage_attention_varlen(16, 16, 16, 0, nseq, H, Hkv, D, None, None, 100, 100, tq, tk, 8, 8, 8, 8, 8, 8, 0.0,
                                  0, 16, 8, 8, None, None, 0, None, None)
     assert rc == _lib.SAGE_ERR_INVALID and b"cu_seqlens" in L.sage_last_error()
+
+
+def test_host_chunk_plan_covers_every_head_in_whole_groups():
+    """sage_attention_host's chunk sizes (host arithmetic, 148 SMs assumed without a GPU): in order they cover
+    the H query heads exactly, each a whole number of GQA groups and at most the reported chunk size; the
+    tapered ends only shrink chunks."""
+    L = _lib.lib()
+    cases = [(1, 40, 40, 32760, 128, 0), (1, 40, 40, 32760, 128, 6), (1, 24, 24, 67576, 128, 0),
+             (4, 32, 8, 8192, 128, 0), (4, 32, 8, 8192, 128, 12), (1, 24, 24, 4608, 128, 0),
+             (2, 7, 7, 3000, 64, 3), (1, 1, 1, 128, 256, 0), (1, 64, 4, 16384, 96, 32)]
+    for B, H, Hkv, S, D, hpc in cases:
+        hg = L.sage_host_heads_per_chunk(B, H, Hkv, S, S, D, hpc)
+        n = L.sage_host_chunk_plan(B, H, Hkv, S, S, D, hpc, None, 0)
+        assert hg > 0 and n > 0, (B, H, Hkv, S, D, hpc)
+        sizes = (ctypes.c_int * n)()
+        assert L.sage_host_chunk_plan(B, H, Hkv, S, S, D, hpc, sizes, n) == n
+        sizes = list(sizes)
+        G = H // Hkv
+        assert sum(sizes) == H, (sizes, H)
+        assert all(0 < c <= hg and c % G == 0 for c in sizes), (sizes, hg, G)
+        if hpc > 0:
+            assert hg == min(hpc, H)
+    assert L.sage_host_chunk_plan(1, 32, 8, 4096, 4096, 128, 6, None, 0) == 0   # not a multiple of 4

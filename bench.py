@@ -14,6 +14,8 @@ Prints one JSON line (rank 0):
              kernels chunk by chunk); the unpipelined copy + attention + copy sequence is reported beside it
   roofline   the attention kernel timed alone (CUDA events around sage_attn_fwd) against the dense
              8-bit tensor peak = 2 x the measured bf16 cuBLAS peak in MEASURED_PEAKS.json
+  roofline_quant  the quantiser stage alone (sage_quantize, as sage_attention runs it) against measured HBM
+             bandwidth, with the same launches in series on one stream and the single launch beside it
   cpu_baseline  the reference's own CPU path for this call (sageattention.sageattn on CPU tensors, installed
              unmodified in baseline/_ref: torch SDPA in bf16 on the host cores), full calls, timed in a separate
              process (the --impl reference arm)
@@ -405,7 +407,7 @@ def run_ours(args):
         if strong:  # copies of all ranks together
             h2d, d2h = h2d * world, d2h * world
 
-    # ---- roofline: the attention kernel alone and the quantisers alone (C ABI, same stream), on this rank's heads
+    # ---- roofline: the attention kernel alone and the quantiser stage alone (C ABI), on this rank's heads
     L = _lib.lib()
     if strong:
         q, k, v = (t[:, :, h0:h1].contiguous() for t in (q, k, v))
@@ -439,7 +441,13 @@ def run_ours(args):
                                     *sq, 1.0, q8, qs, k8, ks, v8t, vs, sync, None, st), "quant_qkv")
 
     def quant():
-        # the three launches sage_attention runs at this kv length
+        # the quantiser stage exactly as sage_attention runs it (at this kv length: the separate launches, V's on
+        # a library stream beside Q's and K's)
+        _lib.check(L.sage_quantize(q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, Bq, Hq, Hq, Sq, Sq, Dq, *sq, *sq,
+                                   *sq, 1.0, q8, qs, k8, ks, v8t, vs, sync, None, st), "quantize")
+
+    def quant_serial():
+        # the same launches one after the other on one stream (the three public stage entries)
         _lib.check(L.sage_v_amax(v.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, vs, st), "v_amax")
         _lib.check(L.sage_quant_q(q.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, 1.0, q8, qs, st), "quant_q")
         _lib.check(L.sage_quant_kv(k.data_ptr(), v.data_ptr(), 0, Bq, Sq, Hq, Dq, *sq, *sq, vs, k8, ks, v8t, st),
@@ -464,6 +472,14 @@ def run_ours(args):
     e1.record(stream)
     torch.cuda.synchronize()
     quant_ms = e0.elapsed_time(e1) / args.steps
+    quant_serial()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        quant_serial()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    quant_serial_ms = e0.elapsed_time(e1) / args.steps
     quant_fused()
     torch.cuda.synchronize()
     e0.record(stream)
@@ -529,8 +545,9 @@ def run_ours(args):
             "roofline_quant": {"bound": "hbm", "achieved": quant_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                "frac": quant_gbs / peaks["hbm_gbs"], "ms_per_call": quant_ms,
                                "algorithmic_bytes": quant_bytes,
-                               "kernels": "v_amax + quant_q + quant_kv (algorithmic bytes exclude the amax re-read)",
-                               "ms_single_launch": quant_fused_ms},
+                               "kernels": "sage_quantize: v_amax then the V codes on a library stream beside "
+                                          "quant_q then the K codes (algorithmic bytes exclude the amax re-read)",
+                               "ms_serial_launches": quant_serial_ms, "ms_single_launch": quant_fused_ms},
         }
         if not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline() if world == 1 else None

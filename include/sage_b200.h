@@ -82,6 +82,16 @@ int sage_quant_qkv(const void* q, const void* k, const void* v, int dtype, int B
                    int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
                    float* vs, int* sync, int* status, void* stream);
 
+/* The quantiser stage of sage_attention (_attention.py:121-131), same arguments and outputs as
+ * sage_quant_qkv: the single launch for kv lengths up to 6144 with D <= 128, otherwise the separate launches,
+ * with the V channel amax and the V codes on a library-owned stream beside the Q and K codes on `stream`
+ * (joined back into `stream` before the call returns; one stream while `stream` is being captured into a
+ * graph).  The outputs are identical either way. */
+int sage_quantize(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                  int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                  int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
+                  float* vs, int* sync, int* status, void* stream);
+
 /* Replaces the attention launch (_attention.py:133-139; kernel make_sage_r2.py:54-269): out[b, s, h, :]
  * (element strides osb, oss, osh) in out_dtype; optional lse [B, H, Sq] (natural log of the softmax
  * denominator of the dequantised logits); causal is bottom-right aligned.  `status` (nullable) is a

@@ -146,6 +146,31 @@ static VarlenWorkspace carve_varlen(void* base, int nseq, int H, int Hkv, int to
 // D256: 0.470 vs 0.245 ms; B1 H16 S16384 D64: 0.073 vs 0.065 ms).
 static bool use_fused_quantiser(int Skv, int D) { return Skv <= 6144 && D <= 128; }
 
+// Per-device side stream of the separate quantiser launches and the events of its fork and join: the V
+// channel amax and the V codes (memory-bound) run on it beside the Q and K codes (bound by the rotation's
+// instruction stream) on the caller's stream, so that the two kinds share the SMs.
+struct QuantFork {
+  bool ready = false;
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static std::mutex g_fork_mu;
+static QuantFork g_fork[64];
+
+// Called with g_fork_mu held; null if the stream or events cannot be created.
+static QuantFork* quant_fork_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  QuantFork& f = g_fork[dev];
+  if (f.ready) return &f;
+  if (cudaStreamCreateWithFlags(&f.side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&f.fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&f.join, cudaEventDisableTiming) != cudaSuccess)
+    return nullptr;
+  f.ready = true;
+  return &f;
+}
+
 // math.isclose(a, b, rel_tol=1e-6) of the reference's fold test (_attention.py:130)
 static bool isclose_rel(double a, double b, double rel) {
   return std::fabs(a - b) <= rel * std::fmax(std::fabs(a), std::fabs(b));
@@ -317,6 +342,74 @@ int sage_attn_fwd_chunked(const int8_t* q8, const float* qs, const int8_t* k8, c
                          causal, q_row0, chunk_rows, n_chunks, osb, oss, osh, lse, status, stream);
 }
 
+int sage_quantize(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,
+                  int D, int64_t qsb, int64_t qss, int64_t qsh, int64_t ksb, int64_t kss, int64_t ksh, int64_t vsb,
+                  int64_t vss, int64_t vsh, float fold, int8_t* q8, float* qs, int8_t* k8, float* ks, uint8_t* v8t,
+                  float* vs, int* sync, int* status, void* stream) {
+  NvtxRange nvtx("sage_quantize");
+  g_error[0] = 0;
+  if (use_fused_quantiser(Skv, D))
+    return sage_quant_qkv(q, k, v, dtype, B, H, Hkv, Sq, Skv, D, qsb, qss, qsh, ksb, kss, ksh, vsb, vss, vsh, fold,
+                          q8, qs, k8, ks, v8t, vs, sync, status, stream);
+  int rc = check_common(dtype, B, Sq, H, D);
+  if (rc == SAGE_OK) rc = check_common(dtype, B, Skv, Hkv, D);
+  if (rc == SAGE_OK && H % Hkv != 0) {
+    set_error("heads %d must be a multiple of kv heads %d", H, Hkv);
+    rc = SAGE_ERR_UNSUPPORTED;
+  }
+  if (rc == SAGE_OK) rc = check_input(q, qsb, qss, qsh, "q");
+  if (rc == SAGE_OK) rc = check_input(k, ksb, kss, ksh, "k");
+  if (rc == SAGE_OK) rc = check_input(v, vsb, vss, vsh, "v");
+  if (rc == SAGE_OK && (!aligned16(q8) || !aligned16(k8) || !aligned16(v8t) || qs == nullptr || ks == nullptr ||
+                        vs == nullptr)) {
+    set_error("q8 / k8 / v8t must be 16-byte aligned, qs, ks and vs non-null");
+    rc = SAGE_ERR_INVALID;
+  }
+  if (rc != SAGE_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const Strides3 sq{qsb, qss, qsh}, sk{ksb, kss, ksh}, sv{vsb, vss, vsh};
+  // One stream while a graph is being captured, and in debug builds (their store checks read one table of
+  // the buffers the current launches may write).
+  bool overlap = true;
+#ifdef SAGE_DEBUG
+  overlap = false;
+#endif
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) overlap = false;
+  std::unique_lock<std::mutex> lock(g_fork_mu, std::defer_lock);
+  QuantFork* F = nullptr;
+  if (overlap) {
+    lock.lock();
+    F = quant_fork_for_current_device();
+  }
+  if (F == nullptr) {
+    rc = launch_v_amax(v, dtype, B, Skv, Hkv, D, sv, vs, s);
+    if (rc == SAGE_OK) rc = launch_quant_q(q, dtype, B, Sq, H, D, sq, fold, q8, qs, s);
+    if (rc == SAGE_OK) rc = launch_quant_kv(k, v, dtype, B, Skv, Hkv, D, sk, sv, vs, k8, ks, v8t, s);
+    return rc;
+  }
+  cudaError_t e = cudaEventRecord(F->fork, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(F->side, F->fork, 0);
+  if (e != cudaSuccess) {
+    set_error("quantiser fork: %s", cudaGetErrorString(e));
+    return SAGE_ERR_LAUNCH;
+  }
+  int rc_side = launch_v_amax(v, dtype, B, Skv, Hkv, D, sv, vs, F->side);
+  if (rc_side == SAGE_OK)
+    rc_side = launch_quant_kv(k, v, dtype, B, Skv, Hkv, D, sk, sv, vs, k8, ks, v8t, F->side, Segs(), kQuantV);
+  rc = launch_quant_q(q, dtype, B, Sq, H, D, sq, fold, q8, qs, s);
+  if (rc == SAGE_OK) rc = launch_quant_kv(k, v, dtype, B, Skv, Hkv, D, sk, sv, vs, k8, ks, v8t, s, Segs(), kQuantK);
+  // the join is enqueued whatever failed, so that the caller's stream never runs ahead of the side stream
+  e = cudaEventRecord(F->join, F->side);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, F->join, 0);
+  if (rc == SAGE_OK) rc = rc_side;
+  if (rc == SAGE_OK && e != cudaSuccess) {
+    set_error("quantiser join: %s", cudaGetErrorString(e));
+    rc = SAGE_ERR_LAUNCH;
+  }
+  return rc;
+}
+
 size_t sage_workspace_bytes(int B, int H, int Hkv, int Sq, int Skv, int D) {
   if (sage_qk_row_bytes(D) == 0 || B <= 0 || H <= 0 || Hkv <= 0 || Sq <= 0 || Skv <= 0) return 0;
   return carve(nullptr, B, H, Hkv, Sq, Skv, D).bytes;
@@ -343,16 +436,8 @@ int sage_attention(const void* q, const void* k, const void* v, int dtype, int B
   if (sm_scale > 0.0 && !isclose_rel(sm_scale, 1.0 / std::sqrt((double)D), 1e-6))
     fold = (float)(sm_scale * std::sqrt((double)D));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (use_fused_quantiser(Skv, D)) {
-    rc = sage_quant_qkv(q, k, v, dtype, B, H, Hkv, Sq, Skv, D, qsb, qss, qsh, ksb, kss, ksh, vsb, vss, vsh, fold,
-                        w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, w.sync, status, s);
-  } else {
-    rc = sage_v_amax(v, dtype, B, Skv, Hkv, D, vsb, vss, vsh, w.vs, s);
-    if (rc == SAGE_OK) rc = sage_quant_q(q, dtype, B, Sq, H, D, qsb, qss, qsh, fold, w.q8, w.qs, s);
-    if (rc == SAGE_OK)
-      rc = sage_quant_kv(k, v, dtype, B, Skv, Hkv, D, ksb, kss, ksh, vsb, vss, vsh, w.vs, w.k8, w.ks, w.v8t, s);
-  }
+  int rc = sage_quantize(q, k, v, dtype, B, H, Hkv, Sq, Skv, D, qsb, qss, qsh, ksb, kss, ksh, vsb, vss, vsh, fold,
+                         w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, w.sync, status, s);
   if (rc == SAGE_OK)
     rc = sage_attn_fwd(w.q8, w.qs, w.k8, w.ks, w.v8t, w.vs, out, dtype, B, H, Hkv, Sq, Skv, D, causal, osb, oss, osh,
                        lse, status, s);

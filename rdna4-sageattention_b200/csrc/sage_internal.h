@@ -67,10 +67,12 @@ int launch_v_amax(const void* v, int dtype, int B, int S, int H, int D, Strides3
                   const Segs& sg = Segs());
 int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides3 st, float fold, int8_t* q8,
                    float* qs, cudaStream_t stream);
-// Varlen (sg.cu set): B is the number of sequences and S the longest key length.
+// Varlen (sg.cu set): B is the number of sequences and S the longest key length.  Dense calls may run the K
+// part (codes, block scales) and the V part (codes) alone; varlen calls always run both.
+enum : int { kQuantK = 1, kQuantV = 2 };
 int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
                     const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream,
-                    const Segs& sg = Segs());
+                    const Segs& sg = Segs(), int parts = kQuantK | kQuantV);
 
 // V amax, Q, K and V quantisation of a dense call in one launch (the single-launch quantiser).  `vs` is
 // [B, Hkv, D] and `sync` holds quant_fused_sync_ints(B, Hkv) ints; both are zeroed by the launcher

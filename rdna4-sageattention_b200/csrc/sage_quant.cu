@@ -799,45 +799,51 @@ static int quant_q_t(const void* q, int B, int S, int H, Strides3 st, float fold
   return kStatusOk;
 }
 
+// parts (dense calls): kQuantK = K codes and block scales, kQuantV = V codes, both = the whole stage; varlen
+// calls run both in one kernel.
 template <int D, typename T>
 static int quant_kv_t(const void* k, const void* v, int B, int S, int H, Strides3 sk, Strides3 sv, const float* vs,
-                      int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
+                      int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg, int parts) {
   const int spad = (int)kv_pad(S);  // varlen: S is the longest sequence
+  const bool do_k = sg.cu != nullptr || (parts & kQuantK), do_v = sg.cu != nullptr || (parts & kQuantV);
   {
     // k8 [planes, pitch, DK], ks [planes, pitch / 32], v8t [planes, D, pitch]
     constexpr uint64_t DK = D == 64 ? 64 : (D == 256 ? 256 : 128);
     const uint64_t rows = sg.cu != nullptr ? (uint64_t)H * sg.pad_total : (uint64_t)B * H * spad;
-    if (register_outputs(stream, {{k8, rows * DK}, {ks, rows / kKvBlock * sizeof(float)}, {v8t, rows * D}}) !=
-        kStatusOk)
-      return kStatusLaunch;
+    const int rc = do_k && do_v ? register_outputs(stream, {{k8, rows * DK}, {ks, rows / kKvBlock * sizeof(float)},
+                                                            {v8t, rows * D}})
+                   : do_k       ? register_outputs(stream, {{k8, rows * DK}, {ks, rows / kKvBlock * sizeof(float)}})
+                                : register_outputs(stream, {{v8t, rows * D}});
+    if (rc != kStatusOk) return kStatusLaunch;
   }
   const T* kp = reinterpret_cast<const T*>(k);
   const T* vp = reinterpret_cast<const T*>(v);
   for (int bh0 = 0; bh0 < B * H; bh0 += kMaxGridY) {
-    if constexpr (D == 128 || D == 256) {
-      if (sg.cu == nullptr) {
-        constexpr int rpb = kRows / rows_tpr<D>();
-        dim3 grid2((spad + rpb - 1) / rpb, min(kMaxGridY, B * H - bh0));
-        // K (rotation, codes, block scales) and V (codes, transposed) in two kernels
-        quant_kv_pair_kernel<D, T, false><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
-        if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
-        dim3 grid3((spad + 127) / 128, min(kMaxGridY, B * H - bh0));
-        quant_v_tile_kernel<D, T><<<grid3, 256, 0, stream>>>(vp, S, H, sv, vs, v8t, bh0);
-        if (check_launch("quant_v") != kStatusOk) return kStatusLaunch;
-        continue;
-      }
-    }
-    dim3 grid((spad + kRows - 1) / kRows, min(kMaxGridY, B * H - bh0));
+    const int planes = min(kMaxGridY, B * H - bh0);
     if (sg.cu != nullptr) {
+      dim3 grid((spad + kRows - 1) / kRows, planes);
       quant_kv_kernel<D, T, true><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
-    } else {
-      // dense D = 64 / 96: K in the one-thread kernel, V in its own
-      quant_kv_kernel<D, T, false, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg, bh0);
       if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
-      dim3 grid3((spad + 127) / 128, min(kMaxGridY, B * H - bh0));
-      quant_v_tile_kernel<D, T><<<grid3, 256, 0, stream>>>(vp, S, H, sv, vs, v8t, bh0);
+      continue;
     }
-    if (check_launch("quant_kv") != kStatusOk) return kStatusLaunch;
+    // dense: K (rotation, codes, block scales) and V (codes, transposed) in two kernels
+    if (do_k) {
+      if constexpr (D == 128 || D == 256) {
+        constexpr int rpb = kRows / rows_tpr<D>();
+        dim3 grid2((spad + rpb - 1) / rpb, planes);
+        quant_kv_pair_kernel<D, T, false><<<grid2, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, bh0);
+      } else {
+        dim3 grid((spad + kRows - 1) / kRows, planes);
+        quant_kv_kernel<D, T, false, false><<<grid, kRows, 0, stream>>>(kp, vp, S, H, sk, sv, vs, k8, ks, v8t, sg,
+                                                                        bh0);
+      }
+      if (check_launch("quant_k") != kStatusOk) return kStatusLaunch;
+    }
+    if (do_v) {
+      dim3 grid3((spad + 127) / 128, planes);
+      quant_v_tile_kernel<D, T><<<grid3, 256, 0, stream>>>(vp, S, H, sv, vs, v8t, bh0);
+      if (check_launch("quant_v") != kStatusOk) return kStatusLaunch;
+    }
   }
   return kStatusOk;
 }
@@ -1026,8 +1032,9 @@ int launch_quant_q(const void* q, int dtype, int B, int S, int H, int D, Strides
 }
 
 int launch_quant_kv(const void* k, const void* v, int dtype, int B, int S, int H, int D, Strides3 sk, Strides3 sv,
-                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg) {
-  SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream, sg)
+                    const float* vs, int8_t* k8, float* ks, uint8_t* v8t, cudaStream_t stream, const Segs& sg,
+                    int parts) {
+  SAGE_DISPATCH_D(D, quant_kv_t, k, v, B, S, H, sk, sv, vs, k8, ks, v8t, stream, sg, parts)
 }
 
 int launch_quant_fused(const void* q, const void* k, const void* v, int dtype, int B, int H, int Hkv, int Sq, int Skv,

@@ -43,6 +43,9 @@ SIGNATURES = {
     "sage_quant_qkv": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64,
                               _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p,
                               _c_p, _c_p, _c_p, _c_p]),
+    "sage_quantize": (_c_i, [_c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i64, _c_i64, _c_i64,
+                             _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_p, _c_p, _c_p, _c_p, _c_p,
+                             _c_p, _c_p, _c_p, _c_p]),
     "sage_attn_fwd": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i,
                              _c_i, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p]),
     "sage_attn_fwd_rows": (_c_i, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_i, _c_i, _c_i, _c_i, _c_i, _c_i,

@@ -49,8 +49,9 @@ def gpu_quant(q, k, v, layout: str, fold: float = 1.0):
     return dict(q8=q8, qs=qs, k8=k8, ks=ks, v8t=v8t, vs=vs, B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D)
 
 
-def gpu_quant_fused(q, k, v, layout: str, fold: float = 1.0):
-    """The single-launch quantiser (sage_quant_qkv) on the same buffers as gpu_quant."""
+def gpu_quant_fused(q, k, v, layout: str, fold: float = 1.0, entry: str = "sage_quant_qkv", sync_stream=True):
+    """The single-launch quantiser (sage_quant_qkv; or `entry` with the same arguments, e.g. sage_quantize, the
+    stage as sage_attention runs it) on the same buffers as gpu_quant, on torch's current stream."""
     L = _lib.lib()
     if layout == "HND":
         B, H, Sq, D = q.shape
@@ -69,13 +70,19 @@ def gpu_quant_fused(q, k, v, layout: str, fold: float = 1.0):
     ks = torch.empty((B, Hkv, spad // 32), device=dev, dtype=torch.float32)
     v8t = torch.full((B, Hkv, D, spad), 0x55, device=dev, dtype=torch.uint8)
     status = torch.zeros(1, device=dev, dtype=torch.int32)
-    _lib.check(L.sage_quant_qkv(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPE_CODE[q.dtype], B, H, Hkv, Sq, Skv, D,
-                                *bsh_strides(q, layout), *bsh_strides(k, layout), *bsh_strides(v, layout), fold,
-                                q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(),
-                                vs.data_ptr(), sync.data_ptr(), status.data_ptr(), stream()), "quant_qkv")
-    torch.cuda.synchronize()
-    return dict(q8=q8, qs=qs, k8=k8, ks=ks, v8t=v8t, vs=vs, B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D,
-                status=int(status.item()), sync=sync.cpu())
+    fn = getattr(L, entry)
+    call = lambda: _lib.check(fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), DTYPE_CODE[q.dtype], B, H, Hkv, Sq, Skv, D,
+                                 *bsh_strides(q, layout), *bsh_strides(k, layout), *bsh_strides(v, layout), fold,
+                                 q8.data_ptr(), qs.data_ptr(), k8.data_ptr(), ks.data_ptr(), v8t.data_ptr(),
+                                 vs.data_ptr(), sync.data_ptr(), status.data_ptr(), stream()), entry)
+    res = dict(q8=q8, qs=qs, k8=k8, ks=ks, v8t=v8t, vs=vs, B=B, H=H, Hkv=Hkv, Sq=Sq, Skv=Skv, D=D, call=call)
+    call()
+    if sync_stream:
+        torch.cuda.synchronize()
+        res.update(status=int(status.item()), sync=sync.cpu())
+    else:
+        res.update(status_tensor=status, sync_tensor=sync)
+    return res
 
 
 def gpu_attn_from_quant(qt: dict, out_dtype: torch.dtype, causal: bool, with_lse: bool = False):

@@ -80,6 +80,17 @@ def test_argument_errors_without_gpu():
     assert rc == _lib.SAGE_ERR_INVALID and b"sync" in L.sage_last_error()   # no sync scratch
     rc = L.sage_quant_qkv(16, 16, 16, 0, 1, 3, 2, *args[4:], 16, None, None)
     assert rc == _lib.SAGE_ERR_UNSUPPORTED      # 3 heads over 2 kv heads
+    # sage_quantize: the single-launch route (kv length 64) checks as sage_quant_qkv does; the separate route
+    # (kv length 8192) checks before it forks or launches anything
+    rc = L.sage_quantize(16, 16, 16, *args, None, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"sync" in L.sage_last_error()
+    long_args = [0, 1, 4, 2, 64, 8192, 128] + [8] * 9 + [1.0]
+    rc = L.sage_quantize(16, 16, 16, *long_args, 16, 16, 16, 16, 16, None, None, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"non-null" in L.sage_last_error()     # vs missing
+    rc = L.sage_quantize(16, ctypes.c_void_p(8), 16, *long_args, 16, 16, 16, 16, 16, 16, None, None, None)
+    assert rc == _lib.SAGE_ERR_INVALID and b"k:" in L.sage_last_error()           # misaligned k
+    rc = L.sage_quantize(16, 16, 16, 0, 1, 3, 2, *long_args[4:], 16, 16, 16, 16, 16, 16, None, None, None)
+    assert rc == _lib.SAGE_ERR_UNSUPPORTED      # 3 heads over 2 kv heads
 
 
 def test_placed_and_chunked_attention_arguments_without_gpu():
